@@ -1,0 +1,198 @@
+/*
+ * fp4x — C ABI of the B200 (sm_100a) decode-GEMV library behind the fp4x vLLM plugin.
+ *
+ * Every entry point takes device pointers, plain integer sizes/strides and a CUDA stream (as void*), launches
+ * asynchronously on that stream and returns FP4X_OK or a negative status; on failure
+ * fp4x_last_error_message() describes it.  Nothing here allocates device memory: calls that need scratch take
+ * a workspace pointer and a counters pointer sized by fp4x_gemv_query().  Counter arrays must be zero before
+ * their first use; the kernels leave them zero again, so one array can be reused by every stream-ordered call.
+ * Calls that share a workspace or a counter array must not overlap on the GPU (use one per stream).
+ *
+ * Layouts are those of the reference kernel library `x/fp4x_kernels.py` (cited as K:<line>):
+ *   activations  bf16 [M, K], row stride x_stride (elements), 16-byte aligned rows
+ *   MXFP8        codes e4m3 [N, K] bytes, scales e8m0 [N, K/32] bytes               (K:9-29)
+ *   W8 g64       codes int8 [N, K], scales fp32 [N, K/64]                           (K:116-144)
+ *   W6 g32       low nibbles [N, K/2], high bit pairs [N, K/4], scales fp16 [N, K/32] (K:151-202)
+ *   NVFP4        e2m1 pairs [N, K/2] (low nibble = even k), e4m3 scales [N, K/16], fp32 global scale (K:73-113)
+ *   INT2         2-bit codes [N, K/4] (bit pairs ORDER), fp16 scales [N, K/group]   (K:304-364)
+ *   BF16         bf16 [N, K]                                                        (K:32-47)
+ * Outputs are [M, N] (row stride out_stride elements) in bf16, f16 or fp32 (out_dtype).
+ * Decode shapes: 1 <= M <= 16.
+ */
+#ifndef FP4X_H_
+#define FP4X_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define FP4X_OK 0
+#define FP4X_ERR_INVALID_ARG (-1)  /* null pointer, bad dtype, M outside 1..16, ... */
+#define FP4X_ERR_UNSUPPORTED (-2)  /* shape or alignment the kernels do not handle */
+#define FP4X_ERR_WORKSPACE (-3)    /* workspace or counter array too small */
+#define FP4X_ERR_CUDA (-4)         /* a CUDA runtime call failed */
+#define FP4X_ERR_DEVICE (-5)       /* a kernel recorded a device-side error (bounded wait expired) */
+
+/* output dtypes */
+#define FP4X_BF16 0
+#define FP4X_F16 1
+#define FP4X_F32 2
+
+/* weight formats (fp4x_gemv_query) */
+#define FP4X_FMT_MX8 0
+#define FP4X_FMT_W8 1
+#define FP4X_FMT_W6 2
+#define FP4X_FMT_NV4 3
+#define FP4X_FMT_BF16 4
+#define FP4X_FMT_INT2 5
+
+/* library version (major*10000 + minor*100 + patch) */
+int fp4x_version(void);
+
+/* message describing the last failing call on this host thread ("" if none) */
+const char* fp4x_last_error_message(void);
+
+/* Reads (and optionally clears) the device error word that bounded waits set when they give up.
+ * Synchronizes `stream`.  Returns FP4X_OK when the word is zero, FP4X_ERR_DEVICE otherwise. */
+int fp4x_device_error(void* stream, int clear, int* code_out);
+
+/* Scratch needed by one GEMV-family call: workspace bytes and number of int32 counters.
+ * fmt: FP4X_FMT_*; batch: number of matrices of a batched call (1 otherwise); group: INT2 scale group. */
+int fp4x_gemv_query(int fmt, int64_t m, int64_t n, int64_t k, int64_t batch, int group, size_t* ws_bytes,
+                    int64_t* n_counters);
+
+/* Replaces mx8_linear (K:65-66 -> _run K:50-62 -> _mx8 K:9-29). */
+int fp4x_mx8_linear(const void* x, int64_t x_stride, const void* w, const void* s, void* out, int64_t out_stride,
+                    int out_dtype, int64_t m, int64_t n, int64_t k, void* ws, size_t ws_bytes, int32_t* counters,
+                    int64_t n_counters, void* stream);
+
+/* Replaces bf16_linear (K:69-70 -> _bg K:32-47). */
+int fp4x_bf16_linear(const void* x, int64_t x_stride, const void* w, void* out, int64_t out_stride, int out_dtype,
+                     int64_t m, int64_t n, int64_t k, void* ws, size_t ws_bytes, int32_t* counters,
+                     int64_t n_counters, void* stream);
+
+/* Replaces nv4_linear (K:102-113 -> _nv4 K:73-99); gs is the fp32 global scale. */
+int fp4x_nv4_linear(const void* x, int64_t x_stride, const void* wp, const void* s, float gs, void* out,
+                    int64_t out_stride, int out_dtype, int64_t m, int64_t n, int64_t k, void* ws, size_t ws_bytes,
+                    int32_t* counters, int64_t n_counters, void* stream);
+
+/* Replaces w8_linear (K:147-148 -> _w8 K:116-135). */
+int fp4x_w8_linear(const void* x, int64_t x_stride, const void* q, const void* s, void* out, int64_t out_stride,
+                   int out_dtype, int64_t m, int64_t n, int64_t k, void* ws, size_t ws_bytes, int32_t* counters,
+                   int64_t n_counters, void* stream);
+
+/* Replaces w6_linear (K:270-271 -> _w6 K:151-176). */
+int fp4x_w6_linear(const void* x, int64_t x_stride, const void* lo, const void* hi, const void* s, void* out,
+                   int64_t out_stride, int out_dtype, int64_t m, int64_t n, int64_t k, void* ws, size_t ws_bytes,
+                   int32_t* counters, int64_t n_counters, void* stream);
+
+/* Replaces int2_logits (K:359-364 -> _int2_head K:304-325, ROW_SCALE off).  `out_bf16` (may be NULL) receives
+ * a bf16 copy of the logits with the same strides. */
+int fp4x_int2_logits(const void* x, int64_t x_stride, const void* p, const void* s, int group, void* out,
+                     int64_t out_stride, int out_dtype, void* out_bf16, int64_t m, int64_t n, int64_t k, void* ws,
+                     size_t ws_bytes, int32_t* counters, int64_t n_counters, void* stream);
+
+/* One W8 matrix of a batched call (the 48 router gates of a decode step, P:258-272 with FP4X_GATE=w8). */
+typedef struct fp4x_w8_item {
+  const void* x;   /* bf16 [M, K] */
+  const void* q;   /* int8 [N, K] */
+  const void* s;   /* fp32 [N, K/64] */
+  void* out;       /* [M, N] */
+} fp4x_w8_item;
+
+/* Runs `count` independent W8 GEMVs of one shape in a single launch.  `items` is a DEVICE array of `count`
+ * fp4x_w8_item, written before the launch is enqueued.  Scratch: fp4x_gemv_query(FP4X_FMT_W8, m, n, k, count). */
+int fp4x_w8_linear_batched(const fp4x_w8_item* items, int64_t count, int64_t x_stride, int64_t out_stride,
+                           int out_dtype, int64_t m, int64_t n, int64_t k, void* ws, size_t ws_bytes,
+                           int32_t* counters, int64_t n_counters, void* stream);
+
+/* Fused hyper-connection down projection (HCFused.down K:503-510 -> _hc_down K:438-467): W8 split-K GEMV of
+ * x [M, K] by q [N, K]; di [M, N] = bf16(sum); bot [M, lr] = bf16(t * sigmoid(t)), t = bf16(di / hc).
+ * Scratch: fp4x_gemv_query(FP4X_FMT_W8, m, n, k, 1). */
+int fp4x_hc_down(const void* x, int64_t x_stride, const void* q, const void* s, void* di, void* bot, int64_t m,
+                 int64_t n, int64_t k, int64_t lr, int64_t hc, void* ws, size_t ws_bytes, int32_t* counters,
+                 int64_t n_counters, void* stream);
+
+/* Fused hyper-connection up projection (HCFused.up K:519-526 -> _hc_up K:470-493): W8 GEMV of bot [M, K] by the
+ * stream-interleaved rows qi [hc*H, K] (HCFused.interleave_up K:513-517); out [M, H] =
+ * bf16(sum_s bf16(nrm[m, s*H + j] * bf16(sigmoid(bf16(g_s)))) / hc), streams summed pairwise.
+ * Requires hc * bj == 16 or 32. */
+int fp4x_hc_up(const void* bot, int64_t bot_stride, const void* qi, const void* si, const void* nrm,
+               int64_t nrm_stride, void* out, int64_t m, int64_t n, int64_t k, int64_t hc, int64_t bj, void* stream);
+
+/* The unfused W8 mixer route (P:231-247): down GEMV + cast, scaled SiLU, up GEMV on the original row order
+ * (qu/su), gate-mean — four launches whose arithmetic equals fp4x_hc_down + fp4x_hc_up bit for bit.
+ * g: bf16 scratch [M, n_up].  Scratch: fp4x_gemv_query(FP4X_FMT_W8, m, n_down, k, 1). */
+int fp4x_hc_mixer_unfused(const void* x, int64_t x_stride, const void* qd, const void* sd, const void* qu,
+                          const void* su, void* di, void* bot, void* g, void* out, int64_t m, int64_t n_down,
+                          int64_t k, int64_t lr, int64_t hc, int64_t n_up, void* ws, size_t ws_bytes,
+                          int32_t* counters, int64_t n_counters, void* stream);
+
+
+/* ---------------------------------------------------------------------------------------------------------
+ * LM heads
+ * Top-C order is total: value descending, then index ascending.  Selected index lists are written in ascending
+ * index order.  Rows are limited to V <= 262144 and C <= 4096.
+ * --------------------------------------------------------------------------------------------------------- */
+
+/* Scratch of fp4x_topk for m rows. */
+int fp4x_topk_query(int64_t m, int64_t v, int64_t c, size_t* ws_bytes, int64_t* n_counters);
+
+/* Exact top-c per row of fp32 values [m, v] (replaces torch.topk at P:318,377 on the coarse logits).
+ * idx_out [m, c] int32; val_out [m, c] (may be NULL) receives the selected values. */
+int fp4x_topk(const float* vals, int64_t ld, int64_t m, int64_t v, int64_t c, int32_t* idx_out, int64_t idx_ld,
+              float* val_out, int64_t val_ld, void* ws, size_t ws_bytes, int32_t* counters, int64_t n_counters,
+              void* stream);
+
+/* Replaces refine_mx8_ (K:384-388 -> _refine_mx8 K:367-381): exact fp32 dots of the MXFP8 rows idx[m, c]
+ * (int32, or int64 when idx64) with x[m]; out[m, idx[m, c]] = cast(value) when out != NULL (in place into the
+ * coarse logits) and exact_out[m, c] = value when exact_out != NULL. */
+int fp4x_refine_mx8(void* out, int64_t out_ld, int out_dtype, const void* x, int64_t x_ld, const void* idx, int idx64,
+                    int64_t idx_ld, const void* w, const void* s, int64_t m, int64_t c, int64_t k, float* exact_out,
+                    int64_t exact_ld, void* stream);
+
+/* Replaces refine_nv4 (K:412-417 -> _refine_nv4 K:391-409): out[m, c] = gs * sum_k bf16(e2m1 * s) * x. */
+int fp4x_refine_nv4(float* out, int64_t out_ld, const void* x, int64_t x_ld, const void* idx, int idx64, int64_t idx_ld,
+                    const void* wp, const void* s, float gs, int64_t m, int64_t c, int64_t k, void* stream);
+
+/* out[m] = the index (from idx) of the largest value in vals[m, 0:c]; equal values: the smaller index. */
+int fp4x_argmax_candidates(const float* vals, int64_t ld, const int32_t* idx, int64_t idx_ld, int64_t m, int64_t c,
+                           int32_t* out, void* stream);
+
+/* Scratch of fp4x_fast_head / fp4x_draft_head. */
+int fp4x_fast_head_query(int64_t m, int64_t v, int64_t k, int64_t c, int group, size_t* ws_bytes,
+                         int64_t* n_counters);
+
+/* The fast target head (P:370-378): INT2 coarse logits over v rows, exact top-c, exact MXFP8 rescore.
+ * full_bf16 [m, v] (contiguous) receives coarse bf16 logits with the c exact values scattered in;
+ * idx_out / exact_out / coarse_out [m, c] and argmax_out [m] are optional (NULL to skip). */
+int fp4x_fast_head(const void* x, int64_t x_ld, const void* p, const void* s, int group, const void* w8,
+                   const void* s8, int64_t m, int64_t v, int64_t k, int64_t c, void* full_bf16, int64_t full_ld,
+                   int32_t* idx_out, float* exact_out, float* coarse_out, int32_t* argmax_out, void* ws,
+                   size_t ws_bytes, int32_t* counters, int64_t n_counters, void* stream);
+
+/* The draft head (P:315-327): INT2 coarse logits over the v draft rows, top-c, exact NVFP4 rescore
+ * (idx_out [m, c] draft-row indices, vals_out [m, c] fp32).  When full_bf16 and ids (int64 [v], draft row ->
+ * vocab id) are given, full_bf16 [m, full_ld] is filled with -inf and the c values are scattered at ids[idx]. */
+int fp4x_draft_head(const void* x, int64_t x_ld, const void* p, const void* s, int group, const void* wp,
+                    const void* sn, float gs, int64_t m, int64_t v, int64_t k, int64_t c, int32_t* idx_out,
+                    float* vals_out, const int64_t* ids, void* full_bf16, int64_t full_ld, int64_t full_v, void* ws,
+                    size_t ws_bytes, int32_t* counters, int64_t n_counters, void* stream);
+
+/* Merge of a vocab-sharded head (no reference counterpart: the reference runs TP=1; this is the exchange step
+ * after an all-gather of every shard's candidates).  coarse / exact / gidx are [parts][m][c] (gidx = global
+ * vocab ids); writes the global top-c by coarse value (idx_out ascending, coarse_out optional, exact_out) and
+ * argmax_out [m] = the exact argmax among them. */
+int fp4x_head_merge(const float* coarse, const float* exact, const int32_t* gidx, int64_t parts, int64_t m, int64_t c,
+                    int64_t v, int32_t* idx_out, float* coarse_out, float* exact_out, int32_t* argmax_out,
+                    void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FP4X_H_ */

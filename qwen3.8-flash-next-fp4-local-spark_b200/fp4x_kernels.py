@@ -1,0 +1,582 @@
+"""fp4x decode kernel library for B200 (sm_100a): drop-in replacement for the reference plugin's `fp4x_kernels`.
+
+Same public names, call signatures and packed weight layouts as the reference module (`x/fp4x_kernels.py`,
+cited K:<line>); the Triton bodies are replaced by hand-written sm_100a CUDA kernels in libfp4x.so, reached
+through the C ABI in include/fp4x.h (see fp4x_native.py).  The Triton tile configurations (`cfg`, `BN`, `BK`,
+`nw`, ...) are still accepted so that callers are unchanged; the native kernels plan their own launch from the
+shape and the device.
+
+Numerics
+* Products are exact and sums are fp32, as in the reference.  MXFP8, NVFP4, INT2 and BF16 weights are
+  multiplied exactly as the reference forms them (bf16-rounded dequantized weights).  W8 and W6 apply the group
+  scale to each group's fp32 partial sum (exact q * s instead of bf16(q * s)); the difference is the bf16
+  rounding of the weight (<= 2^-9 relative per weight).
+* Activations are converted to f16 with a power-of-two scale per token and K-panel for the fp8/int weight
+  formats (exact for every element within 2^31 of the panel maximum) and stay bf16 for BF16/INT2 weights.
+
+Weight preparation (the quantizers and dequantizers) runs in torch on the weights' device and reproduces the
+reference's packing bit for bit.
+"""
+from __future__ import annotations
+
+import torch
+
+import fp4x_native as N
+
+# K:327-328: element j of each 4-group lives in bit pair ORDER[j]
+ORDER = (0, 2, 1, 3)
+_AWQ_LOG = []  # alpha chosen by each quantize_w6_awq call (K:253-254)
+_E2M1 = None
+_E2M1_VALUES = (0.0, 0.5, 1.0, 1.5, 2.0, 3.0, 4.0, 6.0)
+
+
+# ----------------------------------------------------------------------------------------------------------
+# argument plumbing
+# ----------------------------------------------------------------------------------------------------------
+
+def _act(x2):
+    """bf16 activations with 16-byte aligned rows and unit column stride."""
+    if x2.dtype != torch.bfloat16:
+        x2 = x2.to(torch.bfloat16)
+    if x2.stride(-1) != 1 or x2.stride(0) % 8 or x2.data_ptr() % 16:
+        x2 = x2.contiguous()
+        if x2.data_ptr() % 16:
+            x2 = x2.clone()
+    return x2
+
+
+def _rows(t):
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def _u8(t):
+    return t.view(torch.uint8) if t.dtype != torch.uint8 and t.element_size() == 1 else t
+
+
+def _chunks(m):
+    for a in range(0, m, 16):
+        yield a, min(m, a + 16)
+
+
+def _linear(fmt, fn, x2, planes, n, k, out_dtype, extra=(), group=16, post_args=()):
+    """Shared driver of the single-matrix GEMVs: M <= 16 per launch (larger M is split)."""
+    x2 = _act(x2)
+    m = x2.shape[0]
+    out = torch.empty((m, n), dtype=out_dtype, device=x2.device)
+    if m == 0:
+        return out
+    st = N.stream_of(x2)
+    for a, b in _chunks(m):
+        xs = x2[a:b]
+        mm = b - a
+        ws, cnt = N.scratch(fmt, mm, n, k, x2.device, 1, group)
+        o = out[a:b]
+        N.call(fn, N.ptr(xs), xs.stride(0), *[N.ptr(p) for p in planes], *post_args, N.ptr(o), o.stride(0),
+               N.dtype_code(out_dtype), *extra, mm, n, k, *N.scratch_args(ws, cnt), st)
+    return out
+
+
+# ----------------------------------------------------------------------------------------------------------
+# dense decode GEMVs
+# ----------------------------------------------------------------------------------------------------------
+
+def mx8_linear(x2, w8, s, cfg=None, out_dtype=torch.bfloat16):
+    """out = x2 . deq(w8)^T with MXFP8 weights: e4m3 codes [N, K] + e8m0 scales [N, K/32] (K:9-29, K:65)."""
+    n, k = w8.shape
+    return _linear(N.FMT_MX8, "fp4x_mx8_linear", x2, (_rows(_u8(w8)), _rows(_u8(s))), n, k, out_dtype)
+
+
+def bf16_linear(x2, w, cfg=None, out_dtype=torch.bfloat16):
+    """BF16-weight GEMV (K:32-47, K:69)."""
+    n, k = w.shape
+    if w.dtype != torch.bfloat16:
+        raise TypeError("bf16_linear expects bf16 weights")
+    return _linear(N.FMT_BF16, "fp4x_bf16_linear", x2, (_rows(w),), n, k, out_dtype)
+
+
+def nv4_linear(x2, wp, s, gs, cfg=(32, 256, 4), out_dtype=torch.bfloat16):
+    """NVFP4: e2m1 pairs [N, K/2] (low nibble = even k), e4m3 scales [N, K/16], fp32 global scale gs
+    (K:73-113)."""
+    n = wp.shape[0]
+    k = wp.shape[1] * 2
+    x2 = _act(x2)
+    m = x2.shape[0]
+    out = torch.empty((m, n), dtype=out_dtype, device=x2.device)
+    if m == 0:
+        return out
+    g = float(gs)
+    st = N.stream_of(x2)
+    wp, s = _rows(wp), _rows(_u8(s))
+    for a, b in _chunks(m):
+        xs, o = x2[a:b], out[a:b]
+        ws, cnt = N.scratch(N.FMT_NV4, b - a, n, k, x2.device)
+        N.call("fp4x_nv4_linear", N.ptr(xs), xs.stride(0), N.ptr(wp), N.ptr(s), g, N.ptr(o), o.stride(0),
+               N.dtype_code(out_dtype), b - a, n, k, *N.scratch_args(ws, cnt), st)
+    return out
+
+
+def w8_linear(x2, q, s, cfg=None, out_dtype=torch.bfloat16):
+    """int8 codes [N, K] with fp32 scales per 64-group [N, K/64] (K:116-148)."""
+    n, k = q.shape
+    return _linear(N.FMT_W8, "fp4x_w8_linear", x2, (_rows(q), _rows(s.float())), n, k, out_dtype)
+
+
+def w6_linear(x2, L, H, S, cfg=None, out_dtype=torch.bfloat16):
+    """6-bit g32: low-nibble plane [N, K/2], high-bit-pair plane [N, K/4], fp16 scales [N, K/32]
+    (K:151-176, K:270)."""
+    n = L.shape[0]
+    k = L.shape[1] * 2
+    return _linear(N.FMT_W6, "fp4x_w6_linear", x2, (_rows(L), _rows(H), _rows(S)), n, k, out_dtype)
+
+
+def int2_logits(x, P, S, N_rows=None, BN=64, BK=512, nw=4, RS=None, out_dtype=torch.float32, out_bf16=None, **kw):
+    """Coarse logits from 2-bit codes [V, K/4] with fp16 group scales [V, K/G] (K:304-325, K:359-364).
+    Values are x . bf16((code - 1.5) * s).  `out_bf16`, if given ([M, V] bf16), also receives a bf16 copy."""
+    if "N" in kw:
+        N_rows = kw.pop("N")
+    if kw:
+        raise TypeError(f"unexpected arguments {sorted(kw)}")
+    if RS is not None:
+        raise NotImplementedError("ROW_SCALE (e4m3 group scales with per-row fp32 scales) is not supported")
+    x = _act(x)
+    m, k = x.shape
+    n = int(P.shape[0] if N_rows is None else N_rows)
+    group = k // S.shape[1]
+    out = torch.empty((m, n), dtype=out_dtype, device=x.device)
+    if m == 0:
+        return out
+    P, S = _rows(P), _rows(S)
+    st = N.stream_of(x)
+    for a, b in _chunks(m):
+        xs, o = x[a:b], out[a:b]
+        ob = out_bf16[a:b] if out_bf16 is not None else None
+        ws, cnt = N.scratch(N.FMT_INT2, b - a, n, k, x.device, 1, group)
+        N.call("fp4x_int2_logits", N.ptr(xs), xs.stride(0), N.ptr(P), N.ptr(S), group, N.ptr(o), o.stride(0),
+               N.dtype_code(out_dtype), N.ptr(ob), b - a, n, k, *N.scratch_args(ws, cnt), st)
+    return out
+
+
+class W8Batch:
+    """Batched W8 GEMVs of one shape in one launch (the router gates, P:258-272 with FP4X_GATE=w8).
+
+    The device pointer table is built once from the given activation/output buffers and weights, so the launch
+    can be captured in a CUDA graph; callers write new activations into the same `xs` buffers."""
+
+    def __init__(self, xs, qs, ss, outs=None, out_dtype=torch.bfloat16):
+        assert len(xs) == len(qs) == len(ss) and len(qs) > 0
+        self.n, self.k = qs[0].shape
+        self.m = xs[0].shape[0]
+        dev = qs[0].device
+        self.xs = [_act(x) for x in xs]
+        for x in self.xs:
+            assert x.shape == self.xs[0].shape and x.stride(0) == self.xs[0].stride(0)
+        self.qs = [_rows(q) for q in qs]
+        self.ss = [_rows(s.float()) for s in ss]
+        self.out_dtype = out_dtype
+        self.outs = outs if outs is not None else [torch.empty((self.m, self.n), dtype=out_dtype, device=dev)
+                                                   for _ in qs]
+        tab = [[x.data_ptr(), q.data_ptr(), s.data_ptr(), o.data_ptr()]
+               for x, q, s, o in zip(self.xs, self.qs, self.ss, self.outs)]
+        self.table = torch.tensor(tab, dtype=torch.int64, device=dev)
+        self.ws, self.cnt = N.scratch(N.FMT_W8, self.m, self.n, self.k, dev, len(qs))
+
+    def run(self):
+        N.call("fp4x_w8_linear_batched", N.ptr(self.table), len(self.qs), self.xs[0].stride(0),
+               self.outs[0].stride(0), N.dtype_code(self.out_dtype), self.m, self.n, self.k,
+               *N.scratch_args(self.ws, self.cnt), N.stream_of(self.table))
+        return self.outs
+
+
+def w8_linear_batched(xs, qs, ss, out_dtype=torch.bfloat16):
+    """Eager convenience wrapper of W8Batch (builds the pointer table on every call)."""
+    return W8Batch(xs, qs, ss, out_dtype=out_dtype).run()
+
+
+# ----------------------------------------------------------------------------------------------------------
+# LM heads: top-C selection and exact rescoring (K:367-417, P:309-378)
+# ----------------------------------------------------------------------------------------------------------
+
+def topk_indices(vals, C):
+    """Exact top-C per row of fp32 values [M, V]: (indices int32 [M, C] in ascending index order, values [M, C]).
+    Order of the selection: value descending, then index ascending."""
+    vals = vals if vals.dtype == torch.float32 else vals.float()
+    vals = _rows(vals)
+    m, v = vals.shape
+    idx = torch.empty((m, C), dtype=torch.int32, device=vals.device)
+    sel = torch.empty((m, C), dtype=torch.float32, device=vals.device)
+    ws, cnt = N.topk_scratch(m, v, C, vals.device)
+    N.call("fp4x_topk", N.ptr(vals), vals.stride(0), m, v, C, N.ptr(idx), C, N.ptr(sel), C, N.ptr(ws), ws.numel(),
+           N.ptr(cnt), cnt.numel(), N.stream_of(vals))
+    return idx, sel
+
+
+def _idx_args(idx):
+    if idx.dtype not in (torch.int32, torch.int64):
+        raise TypeError("candidate indices must be int32 or int64")
+    idx = _rows(idx)
+    return N.ptr(idx), 1 if idx.dtype == torch.int64 else 0, idx.stride(0)
+
+
+def refine_mx8_(out, x, idx, w8, s_u8, BC=16, BK=256, nw=4):
+    """In place: out[m, idx[m, c]] = exact MXFP8 row idx[m, c] . x[m] (fp32 accumulate), K:384-388."""
+    x = _act(x)
+    m, C = idx.shape
+    k = x.shape[1]
+    if m == 0 or C == 0:
+        return out
+    if out.stride(-1) != 1:
+        raise ValueError("out must have unit column stride")
+    pi, i64, ild = _idx_args(idx)
+    N.call("fp4x_refine_mx8", N.ptr(out), out.stride(0), N.dtype_code(out.dtype), N.ptr(x), x.stride(0), pi, i64,
+           ild, N.ptr(_rows(_u8(w8))), N.ptr(_rows(_u8(s_u8))), m, C, k, None, 0, N.stream_of(x))
+    return out
+
+
+def refine_nv4(x, idx, wp, s, gs, BC=16, BK=256, nw=4):
+    """[M, C] exact NVFP4 logits of candidate rows idx[m, c] (fp32 accumulate), K:412-417."""
+    x = _act(x)
+    m, C = idx.shape
+    k = x.shape[1]
+    out = torch.empty((m, C), dtype=torch.float32, device=x.device)
+    if m == 0 or C == 0:
+        return out
+    pi, i64, ild = _idx_args(idx)
+    N.call("fp4x_refine_nv4", N.ptr(out), C, N.ptr(x), x.stride(0), pi, i64, ild, N.ptr(_rows(wp)),
+           N.ptr(_rows(_u8(s))), float(gs), m, C, k, N.stream_of(x))
+    return out
+
+
+def fast_head(h, P, S, w8, s_u8, C=512, out=None):
+    """Fused fast target head (P:370-378): INT2 coarse logits, exact top-C (fp32 coarse values, ties to the lower
+    vocab id), exact MXFP8 rescore scattered into the coarse bf16 logits.
+    Returns (full bf16 [M, V], idx int32 [M, C] ascending, exact fp32 [M, C], argmax int32 [M])."""
+    h = _act(h)
+    m, k = h.shape
+    v = P.shape[0]
+    group = k // S.shape[1]
+    full = out if out is not None else torch.empty((m, v), dtype=torch.bfloat16, device=h.device)
+    idx = torch.empty((m, C), dtype=torch.int32, device=h.device)
+    exact = torch.empty((m, C), dtype=torch.float32, device=h.device)
+    amax = torch.empty((m,), dtype=torch.int32, device=h.device)
+    ws, cnt = N.head_scratch(m, v, k, C, group, h.device)
+    N.call("fp4x_fast_head", N.ptr(h), h.stride(0), N.ptr(_rows(P)), N.ptr(_rows(S)), group, N.ptr(_rows(_u8(w8))),
+           N.ptr(_rows(_u8(s_u8))), m, v, k, C, N.ptr(full), full.stride(0), N.ptr(idx), N.ptr(exact), None,
+           N.ptr(amax), N.ptr(ws), ws.numel(), N.ptr(cnt), cnt.numel(), N.stream_of(h))
+    return full, idx, exact, amax
+
+
+def draft_head(h, P, S, wp, sn, gs, C=64, ids=None, full_vocab=None):
+    """Fused draft head (P:315-327): INT2 coarse logits over the draft rows, top-C, exact NVFP4 rescore.
+    Returns (idx int32 [M, C] ascending draft-row indices, vals fp32 [M, C], full) where full is the
+    [M, full_vocab] bf16 tensor of -inf with vals scattered at ids[idx] when ids/full_vocab are given."""
+    h = _act(h)
+    m, k = h.shape
+    v = P.shape[0]
+    group = k // S.shape[1]
+    idx = torch.empty((m, C), dtype=torch.int32, device=h.device)
+    vals = torch.empty((m, C), dtype=torch.float32, device=h.device)
+    full = None
+    if ids is not None and full_vocab is not None:
+        full = torch.empty((m, full_vocab), dtype=torch.bfloat16, device=h.device)
+        ids = _rows(ids.long())
+    ws, cnt = N.head_scratch(m, v, k, C, group, h.device)
+    N.call("fp4x_draft_head", N.ptr(h), h.stride(0), N.ptr(_rows(P)), N.ptr(_rows(S)), group, N.ptr(_rows(wp)),
+           N.ptr(_rows(_u8(sn))), float(gs), m, v, k, C, N.ptr(idx), N.ptr(vals), N.ptr(ids), N.ptr(full),
+           full_vocab or 0, full_vocab or 0, N.ptr(ws), ws.numel(), N.ptr(cnt), cnt.numel(), N.stream_of(h))
+    return idx, vals, full
+
+
+def head_merge(coarse, exact, gidx, V):
+    """Merge the candidates of a vocab-sharded head: inputs [P, M, C] (coarse fp32, exact fp32, global ids int32)
+    -> (idx int32 [M, C] ascending, exact fp32 [M, C], argmax int32 [M]) of the global top-C by coarse value."""
+    p, m, C = coarse.shape
+    idx = torch.empty((m, C), dtype=torch.int32, device=coarse.device)
+    co = torch.empty((m, C), dtype=torch.float32, device=coarse.device)
+    ex = torch.empty((m, C), dtype=torch.float32, device=coarse.device)
+    amax = torch.empty((m,), dtype=torch.int32, device=coarse.device)
+    N.call("fp4x_head_merge", N.ptr(_rows(coarse)), N.ptr(_rows(exact)), N.ptr(_rows(gidx)), p, m, C, V, N.ptr(idx),
+           N.ptr(co), N.ptr(ex), N.ptr(amax), N.stream_of(coarse))
+    return idx, co, ex, amax
+
+
+# ----------------------------------------------------------------------------------------------------------
+# hyper-connection mixer (K:429-526)
+# ----------------------------------------------------------------------------------------------------------
+
+class HCFused:
+    """Fused W8 hyper-connection mixer (two kernels per mixer): K:496-526.
+
+    The split-K reduction of the down projection is deterministic (fixed-order sum of per-warp partial slots)
+    and self-cleaning; the arrival counters are shared by every mixer, so calls must be stream-ordered, as in
+    the reference."""
+
+    def __init__(self, device, n_down=336, max_m=16, bn=32):
+        self.device = torch.device(device)
+        self.n_down, self.max_m = n_down, max_m
+        # counters are allocated eagerly so that later calls can be captured
+        self.cnt = N.counters(self.device, 1 << 12)
+
+    def down(self, x, q, s, lr, hc, cfg=(32, 512, 4, 4)):
+        x = _act(x)
+        m, k = x.shape
+        n = q.shape[0]
+        di = torch.empty((m, n), dtype=torch.bfloat16, device=x.device)
+        bot = torch.empty((m, lr), dtype=torch.bfloat16, device=x.device)
+        ws, cnt = N.scratch(N.FMT_W8, m, n, k, x.device)
+        N.call("fp4x_hc_down", N.ptr(x), x.stride(0), N.ptr(_rows(q)), N.ptr(_rows(s.float())), N.ptr(di),
+               N.ptr(bot), m, n, k, lr, hc, *N.scratch_args(ws, cnt), N.stream_of(x))
+        return di, bot
+
+    @staticmethod
+    def interleave_up(q, s, hc, bj):
+        """Reorder up rows [HC*H, K] so that each BJ-column tile holds its HC stream rows contiguously
+        (K:513-517): new row (j*HC + s)*BJ + t = old row s*H + j*BJ + t."""
+        n = q.shape[0]
+        h = n // hc
+        perm = torch.arange(n, device=q.device).view(hc, h // bj, bj).transpose(0, 1).reshape(-1)
+        return q.index_select(0, perm).contiguous(), s.index_select(0, perm).contiguous()
+
+    @staticmethod
+    def up(bot, qi, si, normalized, hc, cfg=(8, 64, 8)):
+        bj = cfg[0]
+        bot = _act(bot)
+        m, k = bot.shape
+        n = qi.shape[0]
+        h = n // hc
+        out = torch.empty((m, h), dtype=torch.bfloat16, device=bot.device)
+        nrm = _act(normalized)
+        N.call("fp4x_hc_up", N.ptr(bot), bot.stride(0), N.ptr(_rows(qi)), N.ptr(_rows(si.float())), N.ptr(nrm),
+               nrm.stride(0), N.ptr(out), m, n, k, hc, bj, N.stream_of(bot))
+        return out
+
+
+def hc_mixer_unfused(x, qd, sd, qu, su, lr, hc):
+    """The unfused W8 mixer route (P:231-247): down GEMV + cast, scaled SiLU, up GEMV on the original row
+    order, gate-mean.  Bit-identical to HCFused.down + HCFused.up.  Returns (di, bot, block_input)."""
+    x = _act(x)
+    m, k = x.shape
+    nd, nu = qd.shape[0], qu.shape[0]
+    di = torch.empty((m, nd), dtype=torch.bfloat16, device=x.device)
+    bot = torch.empty((m, lr), dtype=torch.bfloat16, device=x.device)
+    g = torch.empty((m, nu), dtype=torch.bfloat16, device=x.device)
+    out = torch.empty((m, nu // hc), dtype=torch.bfloat16, device=x.device)
+    ws, cnt = N.scratch(N.FMT_W8, m, nd, k, x.device)
+    N.call("fp4x_hc_mixer_unfused", N.ptr(x), x.stride(0), N.ptr(_rows(qd)), N.ptr(_rows(sd.float())),
+           N.ptr(_rows(qu)), N.ptr(_rows(su.float())), N.ptr(di), N.ptr(bot), N.ptr(g), N.ptr(out), m, nd, k, lr,
+           hc, nu, *N.scratch_args(ws, cnt), N.stream_of(x))
+    return di, bot, out
+
+
+# ----------------------------------------------------------------------------------------------------------
+# weight preparation (torch; restates the reference quantizers so the packed bytes are identical)
+# ----------------------------------------------------------------------------------------------------------
+
+def _row_blocks(n, rows):
+    for a in range(0, n, rows):
+        yield a, min(n, a + rows)
+
+
+@torch.no_grad()
+def quantize_w8(w):
+    """Symmetric int8 per 64-group: s = max(amax, 1e-12) / 127, q = clamp(round(w / s), +-127) (K:138-144)."""
+    n, k = w.shape
+    q = torch.empty((n, k), dtype=torch.int8, device=w.device)
+    s = torch.empty((n, k // 64), dtype=torch.float32, device=w.device)
+    for a, b in _row_blocks(n, 4096):
+        grp = w[a:b].float().reshape(b - a, k // 64, 64)
+        sc = grp.abs().amax(dim=-1).clamp_min(1e-12) / 127.0
+        q[a:b] = torch.round(grp / sc.unsqueeze(-1)).clamp(-127, 127).to(torch.int8).reshape(b - a, k)
+        s[a:b] = sc
+    return q, s
+
+
+def _w6_pack(codes):
+    """codes int32 [R, K] in 0..63 -> (low-nibble plane [R, K/2], high-bit-pair plane [R, K/4])."""
+    lo = codes & 15
+    hi = codes >> 4
+    L = (lo[:, 0::2] | (lo[:, 1::2] << 4)).to(torch.uint8)
+    H = hi[:, 0::4] | (hi[:, 1::4] << (2 * ORDER[1])) | (hi[:, 2::4] << (2 * ORDER[2])) | (hi[:, 3::4] << (2 * ORDER[3]))
+    return L, H.to(torch.uint8)
+
+
+def _w6_scale_search(f, qmax, clip, weight=None):
+    """fp16-rounded g32 scales for f [R, G, 32]; with clip > 0, the scale minimising the (weighted) squared error
+    over a grid of clip ratios 0.70..0.98 (K:205-215)."""
+    s = (f.abs().amax(-1, keepdim=True) / qmax).to(torch.float16).float().clamp_min(6.2e-5)
+    if not clip:
+        return s
+
+    def err(sc):
+        d = (torch.round(f / sc).clamp(-qmax - 1, qmax) * sc - f) ** 2
+        return (d if weight is None else d * weight).sum(-1, keepdim=True)
+
+    best, best_s = err(s), s
+    for c in torch.linspace(0.70, 0.98, clip).tolist():
+        cand = (s * c).to(torch.float16).float().clamp_min(6.2e-5)
+        e = err(cand)
+        take = e < best
+        best = torch.where(take, e, best)
+        best_s = torch.where(take, cand, best_s)
+    return best_s
+
+
+@torch.no_grad()
+def quantize_w6(w, qmax=31, clip_search=0):
+    """6-bit g32 (K:179-202): s = max(fp16(amax/qmax), 6.2e-5), codes = clamp(round(w/s), -qmax-1, qmax) + 32.
+    Returns (L [N,K/2] u8, H [N,K/4] u8, S [N,K/32] f16)."""
+    n, k = w.shape
+    L = torch.empty((n, k // 2), dtype=torch.uint8, device=w.device)
+    H = torch.empty((n, k // 4), dtype=torch.uint8, device=w.device)
+    S = torch.empty((n, k // 32), dtype=torch.float16, device=w.device)
+    for a, b in _row_blocks(n, 2048):
+        f = w[a:b].float().view(-1, k // 32, 32)
+        s = _w6_scale_search(f, qmax, clip_search)
+        codes = (torch.round(f / s).clamp(-qmax - 1, qmax).to(torch.int32) + 32).view(-1, k)
+        L[a:b], H[a:b] = _w6_pack(codes)
+        S[a:b] = s.squeeze(-1).to(torch.float16)
+    return L, H, S
+
+
+@torch.no_grad()
+def quantize_w6_awq(w, h, qmax=31, clip=0, alpha=-1.0):
+    """Activation-aware W6 g32 quality probe (K:218-255).  h [K] = mean x^2 per input channel.  The weight is
+    quantized as W * t with t a power of two per input channel (t = a^alpha normalised, a = sqrt(h)); alpha is
+    grid-searched on up to 1024 random rows when negative.  Returns (L, H, S, inv_t bf16 [K])."""
+    n, k = w.shape
+    a = h.float().clamp_min(1e-12).sqrt()
+    a = a / a.mean()
+    hw = (a * a).view(1, k // 32, 32)
+    rows = torch.randperm(n, device=w.device)[:min(n, 1024)]
+
+    def t_for(al):
+        return torch.exp2(torch.round(torch.log2(a ** al / (a ** al).mean())))
+
+    def weighted_err(t, rr):
+        tv = t.view(1, k // 32, 32)
+        f = (w[rr].float() * t).view(-1, k // 32, 32)
+        sc = _w6_scale_search(f, qmax, clip, hw / tv ** 2)
+        d = torch.round(f / sc).clamp(-qmax - 1, qmax) * sc / tv - w[rr].float().view(-1, k // 32, 32)
+        return ((d * d) * hw).sum().item()
+
+    best_a = alpha
+    if alpha < 0:
+        best_a, best_e = 0.0, None
+        for al in [i / 10 for i in range(11)]:
+            e = weighted_err(t_for(al), rows)
+            if best_e is None or e < best_e:
+                best_e, best_a = e, al
+    t = t_for(best_a)
+    tv = t.view(1, k // 32, 32)
+    L = torch.empty((n, k // 2), dtype=torch.uint8, device=w.device)
+    H = torch.empty((n, k // 4), dtype=torch.uint8, device=w.device)
+    S = torch.empty((n, k // 32), dtype=torch.float16, device=w.device)
+    for r0, r1 in _row_blocks(n, 2048):
+        f = (w[r0:r1].float() * t).view(-1, k // 32, 32)
+        s = _w6_scale_search(f, qmax, clip, hw / tv ** 2)
+        codes = (torch.round(f / s).clamp(-qmax - 1, qmax).to(torch.int32) + 32).view(-1, k)
+        L[r0:r1], H[r0:r1] = _w6_pack(codes)
+        S[r0:r1] = s.squeeze(-1).to(torch.float16)
+    _AWQ_LOG.append(best_a)
+    return L, H, S, (1.0 / t).to(torch.bfloat16)
+
+
+@torch.no_grad()
+def mx8_dequant(w8, s_u8, rows=2048):
+    """MXFP8 -> fp32 [N, K]: e4m3 * 2^(s - 127) (K:261-267)."""
+    n, k = w8.shape
+    codes = w8.view(torch.float8_e4m3fn) if w8.dtype == torch.uint8 else w8
+    out = torch.empty((n, k), dtype=torch.float32, device=w8.device)
+    for a, b in _row_blocks(n, rows):
+        scale = torch.exp2(s_u8[a:b].float() - 127).unsqueeze(-1)
+        out[a:b] = (codes[a:b].float().view(b - a, k // 32, 32) * scale).view(b - a, k)
+    return out
+
+
+@torch.no_grad()
+def quantize_mx8(w):
+    """MXFP8 packing of a float matrix (the synthetic-weight recipe; served weights come packed from b12x):
+    e8m0 byte = 127 + ceil(log2(amax32 / 448)), codes = e4m3(w / 2^(byte - 127)).  Not in the reference module.
+    Returns (codes float8_e4m3fn [N, K], scales uint8 [N, K/32])."""
+    n, k = w.shape
+    f = w.float().view(n, k // 32, 32)
+    amax = f.abs().amax(-1)
+    mant, expo = torch.frexp(amax / 448.0)
+    ce = torch.where(mant > 0.5, expo, expo - 1)
+    ce = torch.where(amax == 0, torch.full_like(ce, -127), ce)
+    sbyte = (ce + 127).clamp(0, 254).to(torch.uint8)
+    codes = (f.double() / torch.exp2(ce.double()).unsqueeze(-1)).float().to(torch.float8_e4m3fn).view(n, k)
+    return codes, sbyte
+
+
+@torch.no_grad()
+def quantize_nv4(w, rows=2048):
+    """NVFP4 (K:277-300): gs = max(amax/6/448, 1e-30) (python float), block scale = e4m3(clamp(amax16/6/gs,
+    2^-9, 448)), magnitudes by nearest e2m1 level with ties to the lower level.  Returns (P, S e4m3, gs)."""
+    global _E2M1
+    n, k = w.shape
+    if _E2M1 is None or _E2M1.device != w.device:
+        _E2M1 = torch.tensor(_E2M1_VALUES, device=w.device)
+    amax_all = 0.0
+    for a, b in _row_blocks(n, rows):
+        amax_all = max(amax_all, w[a:b].float().abs().max().item())
+    gs = max(amax_all / 6.0 / 448.0, 1e-30)
+    P = torch.empty((n, k // 2), dtype=torch.uint8, device=w.device)
+    S = torch.empty((n, k // 16), dtype=torch.float8_e4m3fn, device=w.device)
+    mids = (_E2M1[1:] + _E2M1[:-1]) / 2
+    for a, b in _row_blocks(n, rows):
+        f = w[a:b].float().view(-1, k // 16, 16)
+        blk = (f.abs().amax(-1, keepdim=True) / 6.0 / gs).clamp(min=2 ** -9, max=448.0).to(torch.float8_e4m3fn)
+        v = (f / (blk.float() * gs)).clamp(-6, 6)
+        code = torch.bucketize(v.abs(), mids) | ((v < 0).to(torch.int64) << 3)
+        code = code.view(-1, k)
+        P[a:b] = (code[:, 0::2] | (code[:, 1::2] << 4)).to(torch.uint8)
+        S[a:b] = blk.view(-1, k // 16)
+    return P, S, gs
+
+
+@torch.no_grad()
+def dequant_nv4(P, S, gs):
+    """[N, K/2] e2m1 pairs + [N, K/16] e4m3 scales -> fp32 [N, K] = v * s * gs (K:420-426)."""
+    lut = torch.tensor(_E2M1_VALUES + tuple(-v for v in _E2M1_VALUES), device=P.device)
+    n = P.shape[0]
+    v = torch.stack([lut[(P & 15).long()], lut[(P >> 4).long()]], -1).view(n, -1)
+    return (v.view(n, -1, 16) * S.float().unsqueeze(-1) * gs).view(n, -1)
+
+
+@torch.no_grad()
+def quantize_int2(weight, scale_fmt="fp16", group=16):
+    """INT2 per group (K:330-351): s = max(amax, 1e-8)/1.5 (fp16, or e4m3 relative to an fp32 row scale),
+    code = clamp(floor(w/s) + 2, 0, 3), value (code - 1.5) * s; 4 codes per byte at bit pairs ORDER.
+    Returns (packed, s) for fp16 scales, (packed, s_e4m3, row_scale) for e4m3."""
+    n, k = weight.shape
+    packed = torch.empty((n, k // 4), dtype=torch.uint8, device=weight.device)
+    sdt = torch.float16 if scale_fmt == "fp16" else torch.float8_e4m3fn
+    scales = torch.empty((n, k // group), dtype=sdt, device=weight.device)
+    rowsc = torch.empty((n,), dtype=torch.float32, device=weight.device)
+    for a, b in _row_blocks(n, 8192):
+        f = weight[a:b].float().view(-1, k // group, group)
+        s = f.abs().amax(-1, keepdim=True).clamp_min(1e-8) / 1.5
+        if scale_fmt == "fp16":
+            s = s.half()
+            sf = s.float()
+        else:
+            rs = s.amax(1, keepdim=True) / 448.0
+            s = (s / rs).to(torch.float8_e4m3fn)
+            sf = s.float() * rs
+            rowsc[a:b] = rs.view(-1)
+        code = (torch.floor(f / sf) + 2).clamp(0, 3).to(torch.uint8).view(-1, k // 4, 4)
+        byte = code[..., 0] << (2 * ORDER[0])
+        for j in range(1, 4):
+            byte = byte | (code[..., j] << (2 * ORDER[j]))
+        packed[a:b] = byte
+        scales[a:b] = s.squeeze(-1)
+    return (packed, scales) if scale_fmt == "fp16" else (packed, scales, rowsc)
+
+
+def dequant_int2(packed, scales):
+    """fp32 (code - 1.5) * s (K:353-357)."""
+    n = packed.shape[0]
+    k = packed.shape[1] * 4
+    codes = torch.stack([(packed >> (2 * ORDER[j])) & 3 for j in range(4)], -1).view(n, k).float() - 1.5
+    g = k // scales.shape[1]
+    return (codes.view(n, k // g, g) * scales.float().unsqueeze(-1)).view(n, k)
