@@ -65,6 +65,11 @@ int fp4x_device_error(void* stream, int clear, int* code_out);
 int fp4x_gemv_query(int fmt, int64_t m, int64_t n, int64_t k, int64_t batch, int group, size_t* ws_bytes,
                     int64_t* n_counters);
 
+/* Diagnostic (no reference counterpart): writes a one-line description of the launch plan the library would use for
+ * a GEMV of this format and shape (panels, chunks, CTAs, stages, shared memory, scratch) into buf. */
+int fp4x_plan_describe(int fmt, int64_t m, int64_t n, int64_t k, int64_t batch, int group, int whole, char* buf,
+                       size_t len);
+
 /* Replaces mx8_linear (K:65-66 -> _run K:50-62 -> _mx8 K:9-29). */
 int fp4x_mx8_linear(const void* x, int64_t x_stride, const void* w, const void* s, void* out, int64_t out_stride,
                     int out_dtype, int64_t m, int64_t n, int64_t k, void* ws, size_t ws_bytes, int32_t* counters,
@@ -98,17 +103,26 @@ int fp4x_int2_logits(const void* x, int64_t x_stride, const void* p, const void*
 
 /* One W8 matrix of a batched call (the 48 router gates of a decode step, P:258-272 with FP4X_GATE=w8). */
 typedef struct fp4x_w8_item {
-  const void* x;   /* bf16 [M, K] */
-  const void* q;   /* int8 [N, K] */
+  const void* x;   /* bf16 [M, K], 16-byte aligned rows */
+  const void* q;   /* int8 [N, K], 16-byte aligned */
   const void* s;   /* fp32 [N, K/64] */
   void* out;       /* [M, N] */
 } fp4x_w8_item;
 
-/* Runs `count` independent W8 GEMVs of one shape in a single launch.  `items` is a DEVICE array of `count`
- * fp4x_w8_item, written before the launch is enqueued.  Scratch: fp4x_gemv_query(FP4X_FMT_W8, m, n, k, count). */
-int fp4x_w8_linear_batched(const fp4x_w8_item* items, int64_t count, int64_t x_stride, int64_t out_stride,
-                           int out_dtype, int64_t m, int64_t n, int64_t k, void* ws, size_t ws_bytes,
-                           int32_t* counters, int64_t n_counters, void* stream);
+/* Bytes of the device table that describes `count` batched W8 matrices. */
+size_t fp4x_w8_batch_table_bytes(int64_t count);
+
+/* Builds the device table of a batched W8 call from a HOST array of `count` items (TMA descriptors of the codes
+ * plus the pointers).  `table` is device memory of fp4x_w8_batch_table_bytes(count) bytes, 64-byte aligned.
+ * Synchronous (one host-to-device copy); run it once, outside any stream capture. */
+int fp4x_w8_batch_prepare(const fp4x_w8_item* items, int64_t count, int64_t n, int64_t k, void* table,
+                          size_t table_bytes);
+
+/* Runs the `count` independent W8 GEMVs of a prepared table in a single launch.
+ * Scratch: fp4x_gemv_query(FP4X_FMT_W8, m, n, k, count). */
+int fp4x_w8_linear_batched(const void* table, int64_t count, int64_t x_stride, int64_t out_stride, int out_dtype,
+                           int64_t m, int64_t n, int64_t k, void* ws, size_t ws_bytes, int32_t* counters,
+                           int64_t n_counters, void* stream);
 
 /* Fused hyper-connection down projection (HCFused.down K:503-510 -> _hc_down K:438-467): W8 split-K GEMV of
  * x [M, K] by q [N, K]; di [M, N] = bf16(sum); bot [M, lr] = bf16(t * sigmoid(t)), t = bf16(di / hc).
@@ -120,7 +134,7 @@ int fp4x_hc_down(const void* x, int64_t x_stride, const void* q, const void* s, 
 /* Fused hyper-connection up projection (HCFused.up K:519-526 -> _hc_up K:470-493): W8 GEMV of bot [M, K] by the
  * stream-interleaved rows qi [hc*H, K] (HCFused.interleave_up K:513-517); out [M, H] =
  * bf16(sum_s bf16(nrm[m, s*H + j] * bf16(sigmoid(bf16(g_s)))) / hc), streams summed pairwise.
- * Requires hc * bj == 16 or 32. */
+ * Requires hc * bj == 16 or 32 and n a multiple of 64. */
 int fp4x_hc_up(const void* bot, int64_t bot_stride, const void* qi, const void* si, const void* nrm,
                int64_t nrm_stride, void* out, int64_t m, int64_t n, int64_t k, int64_t hc, int64_t bj, void* stream);
 

@@ -187,7 +187,7 @@ FP4X_DEV float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 // warp MMA m16n8k16, fp32 accumulate
 // ------------------------------------------------------------------------------------------------------
 FP4X_DEV void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, const float (&c)[4]) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%10,%11,%12,%13};"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
@@ -195,7 +195,7 @@ FP4X_DEV void mma_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32
         "f"(c[3]));
 }
 FP4X_DEV void mma_bf16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1, const float (&c)[4]) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%10,%11,%12,%13};"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])

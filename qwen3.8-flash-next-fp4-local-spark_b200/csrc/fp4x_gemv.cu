@@ -1,7 +1,11 @@
-// Host planner, launchers and C ABI of the GEMV family (MXFP8, W8, W6, NVFP4, BF16, INT2, batched W8 and the
-// fused / unfused hyper-connection mixer).
+// Host planner, TMA descriptors, launchers and C ABI of the GEMV family (MXFP8, W8, W6, NVFP4, BF16, INT2, batched
+// W8 and the fused / unfused hyper-connection mixer).
+#include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <string>
+#include <unordered_map>
+#include <vector>
 
 #include "fp4x_gemv.cuh"
 #include "fp4x_host.h"
@@ -41,8 +45,10 @@ const DeviceFacts& device_facts() {
     DeviceFacts f{};
     cudaDeviceGetAttribute(&f.sms, cudaDevAttrMultiProcessorCount, dev);
     cudaDeviceGetAttribute(&f.smem_optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&f.smem_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
     if (f.sms <= 0) f.sms = 148;
     if (f.smem_optin <= 0) f.smem_optin = 227 * 1024;
+    if (f.smem_sm <= 0) f.smem_sm = 228 * 1024;
     facts[dev & 63] = f;
     have[dev & 63] = true;
   }
@@ -65,8 +71,77 @@ cudaError_t ensure_smem_attr(const void* kernel, int bytes) {
   for (int i = 0; i < n; ++i)
     if (tab[i].k == kernel && tab[i].dev == dev && tab[i].bytes >= bytes) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, (int)cudaSharedmemCarveoutMaxShared);
   if (e == cudaSuccess && n < 512) tab[n++] = Entry{kernel, dev, bytes};
   return e;
+}
+
+// ------------------------------------------------------------------------------------------------------
+// TMA descriptors: 2D [rows, row_bytes] uint8 views, box {inner, 64 rows}, 64B/128B swizzle; cached per device
+// ------------------------------------------------------------------------------------------------------
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+static EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = (EncodeTiledFn)p;
+  });
+  return fn;
+}
+
+static int encode_rows_uncached(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t row_bytes, int inner) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(FP4X_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  const cuuint64_t gdim[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  const cuuint64_t gstride[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {(cuuint32_t)inner, (cuuint32_t)kRB};
+  const cuuint32_t es[2] = {1, 1};
+  const CUtensorMapSwizzle sw = inner == 128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B;
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), gdim, gstride, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FP4X_ERR_UNSUPPORTED, "tensor map encode failed (" + std::to_string((int)r) + ")");
+  return FP4X_OK;
+}
+
+static int encode_rows(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t row_bytes, int inner) {
+  struct Key {
+    uintptr_t p;
+    int64_t rows, rb;
+    int inner;
+    bool operator==(const Key& o) const { return p == o.p && rows == o.rows && rb == o.rb && inner == o.inner; }
+  };
+  struct KeyHash {
+    size_t operator()(const Key& k) const {
+      return std::hash<uintptr_t>()(k.p) ^ (std::hash<int64_t>()(k.rows) * 31) ^ (std::hash<int64_t>()(k.rb) * 131) ^
+             (size_t)k.inner;
+    }
+  };
+  static std::unordered_map<Key, CUtensorMap, KeyHash> cache;
+  static std::mutex mu;
+  const Key key{(uintptr_t)ptr, rows, row_bytes, inner};
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    auto itc = cache.find(key);
+    if (itc != cache.end()) {
+      *tm = itc->second;
+      return FP4X_OK;
+    }
+  }
+  int rc = encode_rows_uncached(tm, ptr, rows, row_bytes, inner);
+  if (rc) return rc;
+  std::lock_guard<std::mutex> lk(mu);
+  if (cache.size() > 16384) cache.clear();
+  cache.emplace(key, *tm);
+  return FP4X_OK;
 }
 
 // ------------------------------------------------------------------------------------------------------
@@ -75,21 +150,15 @@ cudaError_t ensure_smem_attr(const void* kernel, int bytes) {
 enum PlanMode { kStreamK = 0, kWholeTile = 1 };
 
 struct Plan {
-  int NT, RG, RU, MP;
+  int NT, MP;
   int KPW, KP, KC, NCH, CPP, RT, NS, SMAX, whole;
-  int P0, P1, PS, STG, XP;
-  int smem_x, smem_stage, smem_scr, smem_total;
+  int BI0, BI1, NB0, SB, STG, off_p1, off_sc, XP;
+  int smem_x, smem_misc, smem_scr, smem_xraw, smem_total;
   size_t ws_bytes;
   int64_t counters;
 };
 
 static int round_up(int v, int a) { return (v + a - 1) / a * a; }
-static int pitch_for(int bytes, int mod) {
-  if (bytes == 0) return 0;
-  int p = round_up(bytes, 16);
-  while (p % 128 != mod) p += 16;
-  return p;
-}
 
 static double bytes_per_k(int fmt, int group) {
   const FmtGeom G = fmt_geom(fmt);
@@ -98,132 +167,154 @@ static double bytes_per_k(int fmt, int group) {
   return b;
 }
 
+// stage chunk for a panel: plane-0 bytes per row per stage 256 (two 128-byte boxes), 128 or 64 (one box)
+static bool chunk_for(int fmt, int kpw, int& KC, int& BI0, int& NB0) {
+  const FmtGeom G = fmt_geom(fmt);
+  const int pbs[3] = {256, 128, 64};
+  for (int pb : pbs) {
+    const int kc = pb * G.d0 / G.n0;
+    if (kc % G.kmin || kpw % kc) continue;
+    if (fmt == FMT_W6 && pb < 128) continue;  // the high-bit plane needs >= 64-byte boxes
+    if (fmt == FMT_MX8 && kc < 128) continue;  // scale rows of >= 4 bytes per stage
+    KC = kc;
+    BI0 = pb >= 128 ? 128 : 64;
+    NB0 = pb / BI0;
+    return true;
+  }
+  return false;
+}
+
 // returns 0 and fills `pl`, or a negative status
-static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, int group, PlanMode mode, int RG,
+static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, int group, PlanMode mode,
                      int epi_scratch, Plan& pl) {
   if (M < 1 || M > 16) return fail(FP4X_ERR_INVALID_ARG, "M must be in 1..16 (decode shapes)");
   if (N < 1 || K < 1 || batch < 1) return fail(FP4X_ERR_INVALID_ARG, "empty shape");
   if (N > (1 << 30) || K > (1 << 20)) return fail(FP4X_ERR_UNSUPPORTED, "shape too large");
   const FmtGeom G = fmt_geom(fmt);
   if (fmt == FMT_INT2 && group != 16 && group != 32) return fail(FP4X_ERR_UNSUPPORTED, "INT2 group must be 16 or 32");
-  if (K % 64 != 0 || K % G.blk != 0)
-    return fail(FP4X_ERR_UNSUPPORTED, "K=" + std::to_string(K) + " must be a multiple of 64 and of " + std::to_string(G.blk));
-  if (fmt == FMT_MX8 && K % 128 != 0) return fail(FP4X_ERR_UNSUPPORTED, "MXFP8 needs K % 128 == 0");
+  const int kmin = fmt == FMT_MX8 ? 128 : G.kmin;
+  if (K % 64 != 0 || K % kmin != 0)
+    return fail(FP4X_ERR_UNSUPPORTED, "K=" + std::to_string(K) + " must be a multiple of " + std::to_string(kmin > 64 ? kmin : 64));
   const DeviceFacts& dv = device_facts();
   pl.NT = M <= 8 ? 1 : 2;
   pl.MP = 8 * pl.NT;
-  pl.RG = RG;
-  pl.RU = 16 * RG;
-  pl.RT = (int)((N + pl.RU - 1) / pl.RU);
-  const int G_ctas = dv.sms;
-  // INT2 heads always use whole row tiles: each row's fp32 sum then has a fixed order that does not depend on the
+  pl.RT = (int)((N + kRB - 1) / kRB);
+  // INT2 heads always use whole row blocks: each row's fp32 sum then has a fixed order that does not depend on the
   // vocabulary size or the grid, so a vocab-sharded head reproduces the unsharded coarse values bit for bit
-  const bool whole = (mode == kWholeTile || K % 256 != 0 || fmt == FMT_INT2);
+  const bool whole = (mode == kWholeTile || fmt == FMT_INT2);
   pl.whole = whole ? 1 : 0;
-  if (!whole) {
-    // panel width: the activation staging per CTA should stay small next to the CTA's share of the weights
-    const double share = (double)batch * N * K * bytes_per_k(fmt, group) / G_ctas;
-    const double xbudget = share / 4 > 8192 ? share / 4 : 8192;
-    int best = 256;
-    for (int kpw = 256; kpw <= K; kpw += 256) {
-      if (K % kpw) continue;
-      if ((double)kpw * pl.MP * 2 <= xbudget && kpw * pl.MP * 2 <= 96 * 1024) best = kpw;
-    }
-    pl.KPW = best;
-    pl.KP = (int)(K / best);
-    pl.KC = 256;
-    pl.NCH = best / 256;
-  } else {
-    pl.KP = 1;
-    pl.KPW = (int)K;
-    pl.KC = 0;  // chosen below with the stage geometry
-  }
-  const int64_t Up = (int64_t)pl.RT * (whole ? 1 : pl.NCH);
-  int64_t cpp = G_ctas / (pl.KP * batch);
-  if (cpp < 1) cpp = 1;
-  if (!whole && pl.NCH > 1) {
-    // row tiles shared between warps need every warp of a panel to own at least one chunk unit
-    if (cpp * kWarps > Up) cpp = Up / kWarps > 0 ? Up / kWarps : 1;
-    if (cpp * kWarps > Up) return fail(FP4X_ERR_UNSUPPORTED, "too few chunk units for one CTA");
-  } else if (cpp > (Up + 1) / 2) {
-    cpp = (Up + 1) / 2;  // whole row tiles: about two per CTA at least
-  }
-  pl.CPP = (int)cpp;
-  // stage geometry
   const int sd = fmt == FMT_INT2 ? group / 2 : G.sd;
-  pl.XP = (pl.KPW / 16) * 32 + 32;
-  pl.smem_x = 640;
-  pl.smem_scr = round_up(pl.smem_x + pl.MP * pl.XP, 128);
-  const int scr_bytes = epi_scratch ? kWarps * pl.RU * pl.MP * 4 : 0;
-  pl.smem_stage = round_up(pl.smem_scr + scr_bytes, 128);
-  const int cap = dv.smem_optin;
-  auto geom = [&](int kc, int& ns) {
-    const int pb0 = kc * G.n0 / G.d0;
-    const int pb1 = G.n1 ? kc * G.n1 / G.d1 : 0;
-    const int sb = G.sn ? kc * G.sn / sd : 0;
-    pl.P0 = pitch_for(pb0, G.mod0);
-    pl.P1 = pitch_for(pb1, G.mod1);
-    pl.PS = sb;
-    pl.STG = round_up(pl.RU * (pl.P0 + pl.P1 + pl.PS), 128);
-    ns = (cap - pl.smem_stage) / (kWarps * pl.STG);
-    return sb % 4 == 0;
-  };
-  int ns = 0;
-  if (whole) {
-    // largest chunk (a multiple of the decode block dividing K) that still leaves a 3-deep ring, else 2-deep
-    const int step = G.blk > 64 ? G.blk : 64;
-    int pick = 0;
-    for (int want = 3; want >= 2 && !pick; --want)
-      for (int kc = (int)K; kc >= step; kc -= step) {
-        if (K % kc || kc % step) continue;
-        int n2;
-        if (geom(kc, n2) && n2 >= want) { pick = kc; break; }
+  const double wbytes = (double)batch * N * K * bytes_per_k(fmt, group);
+  const int misc = 512;
+  const int scr_bytes = epi_scratch ? kCWarps * 16 * pl.MP * 4 : 0;
+  const int cap1 = dv.smem_optin;
+  const int cap2 = dv.smem_sm / 2 - 2048;  // two CTAs per SM (1 KB reserved per CTA, 1 KB alignment slack)
+
+  bool found = false;
+  double best_score = -1e30;
+  Plan best = pl;
+  for (int kpw = (int)K; kpw >= 64; --kpw) {
+    if (K % kpw) continue;
+    if (whole && kpw != K) break;
+    int KC, BI0, NB0;
+    if (!chunk_for(fmt, kpw, KC, BI0, NB0)) continue;
+    Plan c = pl;
+    c.KPW = kpw;
+    c.KP = (int)(K / kpw);
+    c.KC = KC;
+    c.BI0 = BI0;
+    c.NB0 = NB0;
+    c.NCH = kpw / KC;
+    c.BI1 = G.n1 ? KC * G.n1 / G.d1 : 0;
+    c.SB = G.sn ? KC * G.sn / sd : 0;
+    if (c.SB % 4) continue;
+    c.off_p1 = kRB * NB0 * BI0;
+    c.off_sc = c.off_p1 + kRB * c.BI1;
+    c.STG = round_up(c.off_sc + kRB * c.SB, 1024);
+    c.XP = (kpw / 16) * 32 + 32;
+    const int xbytes = round_up(c.MP * c.XP, 16) + (int)M * kpw * 2;  // permuted panel + raw bf16 panel
+    const int fixed = xbytes + misc + scr_bytes + 1024;
+    for (int cps = 2; cps >= 1; --cps) {
+      const int cap = cps == 2 ? cap2 : cap1;
+      int ns = (cap - fixed) / c.STG;
+      if (ns > kMaxStages) ns = kMaxStages;
+      if (ns < 2 || (cps == 2 && ns < 3)) continue;
+      const double inflight = (double)cps * ns * c.STG;
+      const int ctas = cps * dv.sms;
+      const double share = wbytes / ctas;
+      // score: bytes in flight per SM (up to ~128 KB), minus the relative cost of staging activations per CTA and of
+      // the cross-panel reduction traffic
+      const double x_cost = (double)c.MP * kpw * 2 / (share > 1 ? share : 1);
+      const double red_cost = c.KP > 1 ? (double)c.KP * N * c.MP * 8.0 * batch / wbytes : 0.0;
+      const double score = (inflight < 131072 ? inflight : 131072) / 131072.0 - 0.5 * x_cost - red_cost;
+      if (score > best_score) {
+        best_score = score;
+        c.NS = ns;
+        c.CPP = cps;  // CTAs per SM for now
+        best = c;
+        found = true;
       }
-    if (!pick) return fail(FP4X_ERR_UNSUPPORTED, "shape needs more shared memory than available");
-    pl.KC = pick;
-    pl.NCH = (int)(K / pick);
+      break;
+    }
   }
-  if (!geom(pl.KC, ns)) return fail(FP4X_ERR_UNSUPPORTED, "scale row chunk must be a multiple of 4 bytes");
-  if (ns > kMaxStages) ns = kMaxStages;
-  if (ns < 2) return fail(FP4X_ERR_UNSUPPORTED, "shape needs more shared memory than available (K too large?)");
-  pl.NS = ns;
-  pl.smem_total = pl.smem_stage + kWarps * ns * pl.STG;
-  const int Wp = pl.CPP * kWarps;
-  pl.SMAX = whole ? 1 : (int)((int64_t)(pl.NCH - 1) * Wp / Up) + 2;
-  if (pl.SMAX > Wp) pl.SMAX = Wp;
-  const size_t slot = (size_t)pl.RU * pl.MP * sizeof(float);
+  if (!found) return fail(FP4X_ERR_UNSUPPORTED, "shape needs more shared memory than available");
+  pl = best;
+  const int cps = pl.CPP;
+  const int64_t Up = whole ? (int64_t)pl.RT : (int64_t)pl.RT * pl.NCH;
+  int64_t cpp = (int64_t)cps * dv.sms / (pl.KP * batch);
+  if (cpp < 1) cpp = 1;
+  if (cpp > Up) cpp = Up;  // every CTA owns at least one unit
+  pl.CPP = (int)cpp;
+  pl.smem_x = pl.NS * pl.STG;
+  pl.smem_misc = pl.smem_x + round_up(pl.MP * pl.XP, 16);
+  pl.smem_scr = pl.smem_misc + misc;
+  pl.smem_xraw = pl.smem_scr + round_up(scr_bytes, 16);
+  pl.smem_total = pl.smem_xraw + (int)M * pl.KPW * 2 + 1024;
+  pl.SMAX = whole ? 1 : (int)((int64_t)(pl.NCH - 1) * pl.CPP / Up) + 2;
+  if (pl.SMAX > pl.CPP) pl.SMAX = pl.CPP;
+  const size_t slot = (size_t)kCWarps * 16 * pl.MP * sizeof(float);
+  const bool split = !whole && pl.NCH > 1;
   if (pl.KP > 1)
     pl.ws_bytes = (size_t)batch * pl.KP * pl.RT * pl.SMAX * slot;
-  else if (pl.NCH > 1 && !whole)
-    pl.ws_bytes = (size_t)batch * Wp * 2 * slot;
+  else if (split)
+    pl.ws_bytes = (size_t)batch * pl.CPP * 2 * slot;
   else
     pl.ws_bytes = 0;
-  pl.counters = (pl.KP > 1 || (pl.NCH > 1 && !whole)) ? (int64_t)batch * pl.RT : 0;
+  pl.counters = (pl.KP > 1 || split) ? (int64_t)batch * pl.RT * kCWarps : 0;
   return FP4X_OK;
 }
 
 // ------------------------------------------------------------------------------------------------------
 // launch
 // ------------------------------------------------------------------------------------------------------
-template <int FMT, int NT, int RG, int EPI>
-static int launch_t(const Plan& pl, GemvArgs& a, int64_t batch, cudaStream_t st) {
-  auto kern = gemv_kernel<FMT, NT, RG, EPI>;
+template <int FMT, int NT, int EPI>
+static int launch_t(const Plan& pl, const GemvArgs& a, int64_t batch, cudaStream_t st) {
+  auto kern = gemv_kernel<FMT, NT, EPI>;
   cudaError_t e = ensure_smem_attr((const void*)kern, pl.smem_total);
   if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
   return check_launch(launch_pdl(kern, dim3(pl.CPP, pl.KP, (unsigned)batch), dim3(kThreads), pl.smem_total, st, a),
                       "gemv launch");
 }
 
-template <int FMT, int EPI, int RG>
-static int launch_nt(const Plan& pl, GemvArgs& a, int64_t batch, cudaStream_t st) {
-  return pl.NT == 1 ? launch_t<FMT, 1, RG, EPI>(pl, a, batch, st) : launch_t<FMT, 2, RG, EPI>(pl, a, batch, st);
+template <int FMT, int EPI>
+static int launch_nt(const Plan& pl, const GemvArgs& a, int64_t batch, cudaStream_t st) {
+  return pl.NT == 1 ? launch_t<FMT, 1, EPI>(pl, a, batch, st) : launch_t<FMT, 2, EPI>(pl, a, batch, st);
 }
 
 static void fill_args(const Plan& pl, GemvArgs& a) {
   a.err = dev_error_ptr();
   a.KPW = pl.KPW; a.KP = pl.KP; a.KC = pl.KC; a.NCH = pl.NCH; a.CPP = pl.CPP; a.RT = pl.RT; a.NS = pl.NS;
-  a.SMAX = pl.SMAX; a.whole = pl.whole; a.P0 = pl.P0; a.P1 = pl.P1; a.PS = pl.PS; a.STG = pl.STG; a.XP = pl.XP;
-  a.smem_x = pl.smem_x; a.smem_stage = pl.smem_stage; a.smem_scr = pl.smem_scr;
+  a.SMAX = pl.SMAX; a.whole = pl.whole;
+  a.BI0 = pl.BI0; a.BI1 = pl.BI1; a.NB0 = pl.NB0; a.SB = pl.SB; a.STG = pl.STG;
+  a.off_p1 = pl.off_p1; a.off_sc = pl.off_sc; a.XP = pl.XP;
+  a.smem_x = pl.smem_x; a.smem_misc = pl.smem_misc; a.smem_scr = pl.smem_scr; a.smem_xraw = pl.smem_xraw;
+}
+
+// widest cp.async (16/8/4 bytes) that keeps every scale copy aligned
+static int scale_width(const void* sc, int64_t lds, int SB) {
+  for (int w : {16, 8, 4})
+    if (SB % w == 0 && lds % w == 0 && aligned(sc, w)) return w;
+  return 0;
 }
 
 static int check_scratch(const Plan& pl, void* ws, size_t ws_bytes, int32_t* counters, int64_t n_counters) {
@@ -258,11 +349,11 @@ static int check_rows(const void* p, int64_t row_bytes, const char* what) {
 static int run_gemv(int fmt, const void* x, int64_t x_stride, const void* p0, const void* p1, const void* sc,
                     float post, int group, void* out, void* out2, int64_t out_stride, int out_dtype, int64_t m,
                     int64_t n, int64_t k, void* ws, size_t ws_bytes, int32_t* counters, int64_t n_counters,
-                    void* stream, int epi, PlanMode mode = kStreamK) {
+                    void* stream, int epi, PlanMode mode = kStreamK, int lr = 0, int hc = 0) {
   int rc;
   if ((rc = check_out_dtype(out_dtype))) return rc;
   Plan pl;
-  if ((rc = make_plan(fmt, m, n, k, 1, group, mode, 1, 0, pl))) return rc;
+  if ((rc = make_plan(fmt, m, n, k, 1, group, mode, 0, pl))) return rc;
   if ((rc = check_x(x, x_stride, k))) return rc;
   const FmtGeom G = fmt_geom(fmt);
   const int64_t ld0 = k * G.n0 / G.d0, ld1 = G.n1 ? k * G.n1 / G.d1 : 0;
@@ -270,28 +361,37 @@ static int run_gemv(int fmt, const void* x, int64_t x_stride, const void* p0, co
   const int64_t lds = G.sn ? k * G.sn / sd : 0;
   if ((rc = check_rows(p0, ld0, "weight"))) return rc;
   if (G.n1 && (rc = check_rows(p1, ld1, "weight plane 1"))) return rc;
-  if (G.sn && (!sc || !aligned(sc, 4) || lds % 4)) return fail(FP4X_ERR_UNSUPPORTED, "scales must be 4-byte aligned rows");
+  int scw = 0;
+  if (G.sn) {
+    if (!sc) return fail(FP4X_ERR_INVALID_ARG, "null scales");
+    scw = scale_width(sc, lds, pl.SB);
+    if (!scw) return fail(FP4X_ERR_UNSUPPORTED, "scale rows must be 4-byte aligned");
+  }
   if (!out) return fail(FP4X_ERR_INVALID_ARG, "null output");
   if (out_stride < n) return fail(FP4X_ERR_INVALID_ARG, "out_stride < n");
   if ((rc = check_scratch(pl, ws, ws_bytes, counters, n_counters))) return rc;
-  GemvArgs a = {};
-  a.item = GemvItem{x, (const uint8_t*)p0, (const uint8_t*)p1, (const uint8_t*)sc, out, out2};
-  a.items4 = nullptr;
+  GemvArgs a;
+  std::memset(&a, 0, sizeof(a));
+  if ((rc = encode_rows(&a.tm0, p0, n, ld0, pl.BI0))) return rc;
+  if (G.n1 && (rc = encode_rows(&a.tm1, p1, n, ld1, pl.BI1))) return rc;
+  a.item = GemvItem{x, (const uint8_t*)sc, out, out2};
+  a.batch = nullptr;
   a.M = (int)m; a.N = (int)n; a.K = (int)k;
-  a.x_stride = x_stride; a.ld0 = ld0; a.ld1 = ld1; a.lds = lds;
+  a.x_stride = x_stride; a.lds = lds; a.scw = scw;
   a.out_stride = out_stride; a.out_dtype = out_dtype; a.post = post; a.group = group;
+  a.lr = lr; a.hc = hc;
   a.ws = (float*)ws; a.sem = counters;
   fill_args(pl, a);
   cudaStream_t st = (cudaStream_t)stream;
   switch (fmt) {
-    case FMT_MX8: return launch_nt<FMT_MX8, EPI_STORE, 1>(pl, a, 1, st);
+    case FMT_MX8: return launch_nt<FMT_MX8, EPI_STORE>(pl, a, 1, st);
     case FMT_W8:
-      if (epi == EPI_HC_DOWN) return launch_nt<FMT_W8, EPI_HC_DOWN, 1>(pl, a, 1, st);
-      return launch_nt<FMT_W8, EPI_STORE, 1>(pl, a, 1, st);
-    case FMT_W6: return launch_nt<FMT_W6, EPI_STORE, 1>(pl, a, 1, st);
-    case FMT_NV4: return launch_nt<FMT_NV4, EPI_STORE, 1>(pl, a, 1, st);
-    case FMT_BF16: return launch_nt<FMT_BF16, EPI_STORE, 1>(pl, a, 1, st);
-    case FMT_INT2: return launch_nt<FMT_INT2, EPI_HEAD, 1>(pl, a, 1, st);
+      if (epi == EPI_HC_DOWN) return launch_nt<FMT_W8, EPI_HC_DOWN>(pl, a, 1, st);
+      return launch_nt<FMT_W8, EPI_STORE>(pl, a, 1, st);
+    case FMT_W6: return launch_nt<FMT_W6, EPI_STORE>(pl, a, 1, st);
+    case FMT_NV4: return launch_nt<FMT_NV4, EPI_STORE>(pl, a, 1, st);
+    case FMT_BF16: return launch_nt<FMT_BF16, EPI_STORE>(pl, a, 1, st);
+    case FMT_INT2: return launch_nt<FMT_INT2, EPI_HEAD>(pl, a, 1, st);
   }
   return fail(FP4X_ERR_INVALID_ARG, "bad format");
 }
@@ -333,7 +433,7 @@ using namespace fp4x;
 // ------------------------------------------------------------------------------------------------------
 extern "C" {
 
-int fp4x_version(void) { return 100; }
+int fp4x_version(void) { return 200; }
 
 const char* fp4x_last_error_message(void) { return t_msg.c_str(); }
 
@@ -356,10 +456,24 @@ int fp4x_gemv_query(int fmt, int64_t m, int64_t n, int64_t k, int64_t batch, int
                     int64_t* n_counters) {
   if (fmt < 0 || fmt > 5) return fail(FP4X_ERR_INVALID_ARG, "bad format");
   Plan pl;
-  int rc = make_plan(fmt, m, n, k, batch, group ? group : 16, kStreamK, 1, 0, pl);
+  int rc = make_plan(fmt, m, n, k, batch, group ? group : 16, kStreamK, 0, pl);
   if (rc) return rc;
   if (ws_bytes) *ws_bytes = pl.ws_bytes;
   if (n_counters) *n_counters = pl.counters;
+  return FP4X_OK;
+}
+
+int fp4x_plan_describe(int fmt, int64_t m, int64_t n, int64_t k, int64_t batch, int group, int whole, char* buf,
+                       size_t len) {
+  if (fmt < 0 || fmt > 5 || !buf || len == 0) return fail(FP4X_ERR_INVALID_ARG, "bad argument");
+  Plan pl;
+  int rc = make_plan(fmt, m, n, k, batch, group ? group : 16, whole ? kWholeTile : kStreamK, 0, pl);
+  if (rc) return rc;
+  snprintf(buf, len,
+           "KPW=%d KP=%d KC=%d NCH=%d CPP=%d RT=%d NS=%d STG=%d BI0=%d NB0=%d BI1=%d SB=%d smem=%d whole=%d "
+           "ws=%zu counters=%lld ctas=%lld",
+           pl.KPW, pl.KP, pl.KC, pl.NCH, pl.CPP, pl.RT, pl.NS, pl.STG, pl.BI0, pl.NB0, pl.BI1, pl.SB, pl.smem_total,
+           pl.whole, pl.ws_bytes, (long long)pl.counters, (long long)pl.CPP * pl.KP * batch);
   return FP4X_OK;
 }
 
@@ -405,25 +519,55 @@ int fp4x_int2_logits(const void* x, int64_t x_stride, const void* p, const void*
                   ws, ws_bytes, counters, n_counters, stream, EPI_HEAD);
 }
 
-int fp4x_w8_linear_batched(const fp4x_w8_item* items, int64_t count, int64_t x_stride, int64_t out_stride,
-                           int out_dtype, int64_t m, int64_t n, int64_t k, void* ws, size_t ws_bytes,
-                           int32_t* counters, int64_t n_counters, void* stream) {
-  int rc;
-  if (!items || count < 1 || count > 65535) return fail(FP4X_ERR_INVALID_ARG, "bad item array");
-  if ((rc = check_out_dtype(out_dtype))) return rc;
-  if (x_stride % 8 || x_stride < k || k % 16) return fail(FP4X_ERR_UNSUPPORTED, "activation stride must be a multiple of 8 elements");
+size_t fp4x_w8_batch_table_bytes(int64_t count) { return (size_t)(count > 0 ? count : 0) * sizeof(BatchEntry); }
+
+int fp4x_w8_batch_prepare(const fp4x_w8_item* items, int64_t count, int64_t n, int64_t k, void* table,
+                          size_t table_bytes) {
+  if (!items || count < 1 || count > 65535 || !table) return fail(FP4X_ERR_INVALID_ARG, "bad item array");
+  if (table_bytes < fp4x_w8_batch_table_bytes(count) || !aligned(table, 64))
+    return fail(FP4X_ERR_WORKSPACE, "table too small or not 64-byte aligned (see fp4x_w8_batch_table_bytes)");
+  if (k % 64 || n < 1) return fail(FP4X_ERR_UNSUPPORTED, "K must be a multiple of 64");
   Plan pl;
-  if ((rc = make_plan(FMT_W8, m, n, k, count, 16, kStreamK, 1, 0, pl))) return rc;
+  int rc = make_plan(FMT_W8, 1, n, k, count, 16, kStreamK, 0, pl);
+  if (rc) return rc;
+  std::vector<BatchEntry> host((size_t)count);
+  std::memset(host.data(), 0, host.size() * sizeof(BatchEntry));
+  for (int64_t i = 0; i < count; ++i) {
+    const fp4x_w8_item& it = items[i];
+    if ((rc = check_rows(it.q, k, "weight"))) return rc;
+    if (!it.x || !it.s || !it.out || !aligned(it.x, 16) || !aligned(it.s, 4))
+      return fail(FP4X_ERR_INVALID_ARG, "bad item pointers");
+    if ((rc = encode_rows_uncached(&host[i].tm0, it.q, n, k, pl.BI0))) return rc;
+    host[i].x = it.x;
+    host[i].sc = (const uint8_t*)it.s;
+    host[i].out = it.out;
+  }
+  cudaError_t e = cudaMemcpy(table, host.data(), host.size() * sizeof(BatchEntry), cudaMemcpyHostToDevice);
+  return check_launch(e, "copying the batch table");
+}
+
+int fp4x_w8_linear_batched(const void* table, int64_t count, int64_t x_stride, int64_t out_stride, int out_dtype,
+                           int64_t m, int64_t n, int64_t k, void* ws, size_t ws_bytes, int32_t* counters,
+                           int64_t n_counters, void* stream) {
+  int rc;
+  if (!table || count < 1 || count > 65535) return fail(FP4X_ERR_INVALID_ARG, "bad batch table");
+  if ((rc = check_out_dtype(out_dtype))) return rc;
+  if (x_stride % 8 || x_stride < k) return fail(FP4X_ERR_UNSUPPORTED, "activation stride must be a multiple of 8 elements");
+  Plan pl;
+  if ((rc = make_plan(FMT_W8, m, n, k, count, 16, kStreamK, 0, pl))) return rc;
   if ((rc = check_scratch(pl, ws, ws_bytes, counters, n_counters))) return rc;
-  static_assert(sizeof(fp4x_w8_item) == 4 * sizeof(void*), "item layout is four pointers {x, q, s, out}");
-  GemvArgs a = {};
-  a.items4 = reinterpret_cast<const void* const*>(items);
+  Plan p1;
+  if ((rc = make_plan(FMT_W8, 1, n, k, count, 16, kStreamK, 0, p1))) return rc;
+  if (p1.BI0 != pl.BI0) return fail(FP4X_ERR_UNSUPPORTED, "batch table prepared for a different box width");
+  GemvArgs a;
+  std::memset(&a, 0, sizeof(a));
+  a.batch = reinterpret_cast<const BatchEntry*>(table);
   a.M = (int)m; a.N = (int)n; a.K = (int)k;
-  a.x_stride = x_stride; a.ld0 = k; a.ld1 = 0; a.lds = k / 16;
+  a.x_stride = x_stride; a.lds = k / 16; a.scw = 4;  // item scale pointers are only required to be 4-byte aligned
   a.out_stride = out_stride; a.out_dtype = out_dtype; a.post = 1.f; a.group = 16;
   a.ws = (float*)ws; a.sem = counters;
   fill_args(pl, a);
-  return launch_nt<FMT_W8, EPI_STORE, 1>(pl, a, count, (cudaStream_t)stream);
+  return launch_nt<FMT_W8, EPI_STORE>(pl, a, count, (cudaStream_t)stream);
 }
 
 int fp4x_hc_down(const void* x, int64_t x_stride, const void* q, const void* s, void* di, void* bot, int64_t m,
@@ -431,49 +575,32 @@ int fp4x_hc_down(const void* x, int64_t x_stride, const void* q, const void* s, 
                  int64_t n_counters, void* stream) {
   if (!di || !bot) return fail(FP4X_ERR_INVALID_ARG, "null output");
   if (lr < 1 || lr > n || hc < 1 || hc > 8) return fail(FP4X_ERR_INVALID_ARG, "bad lr/hc");
-  int rc;
-  Plan pl;
-  if ((rc = make_plan(FMT_W8, m, n, k, 1, 16, kStreamK, 1, 0, pl))) return rc;
-  if ((rc = check_x(x, x_stride, k))) return rc;
-  if ((rc = check_rows(q, k, "weight"))) return rc;
-  if ((rc = check_scratch(pl, ws, ws_bytes, counters, n_counters))) return rc;
-  GemvArgs a = {};
-  a.item = GemvItem{x, (const uint8_t*)q, nullptr, (const uint8_t*)s, di, bot};
-  a.M = (int)m; a.N = (int)n; a.K = (int)k;
-  a.x_stride = x_stride; a.ld0 = k; a.lds = k / 16;
-  a.out_stride = n; a.out_dtype = FP4X_BF16; a.post = 1.f; a.group = 16;
-  a.lr = (int)lr; a.hc = (int)hc;
-  a.ws = (float*)ws; a.sem = counters;
-  fill_args(pl, a);
-  return launch_nt<FMT_W8, EPI_HC_DOWN, 1>(pl, a, 1, (cudaStream_t)stream);
-}
-
-static int hc_up_impl(const void* bot, int64_t bot_stride, const void* qi, const void* si, const void* nrm,
-                      int64_t nrm_stride, void* out, int64_t m, int64_t n, int64_t k, int64_t hc, int64_t bj,
-                      void* stream) {
-  int rc;
-  if (!out || !nrm) return fail(FP4X_ERR_INVALID_ARG, "null pointer");
-  if (hc < 1 || hc > 8 || bj < 1 || (hc * bj != 16 && hc * bj != 32) || n % (hc * bj))
-    return fail(FP4X_ERR_UNSUPPORTED, "hc * bj must be 16 or 32 and divide n");
-  const int RG = (int)(hc * bj / 16);
-  Plan pl;
-  if ((rc = make_plan(FMT_W8, m, n, k, 1, 16, kWholeTile, RG, 1, pl))) return rc;
-  if ((rc = check_x(bot, bot_stride, k))) return rc;
-  if ((rc = check_rows(qi, k, "weight"))) return rc;
-  GemvArgs a = {};
-  a.item = GemvItem{bot, (const uint8_t*)qi, nullptr, (const uint8_t*)si, out, nullptr};
-  a.M = (int)m; a.N = (int)n; a.K = (int)k;
-  a.x_stride = bot_stride; a.ld0 = k; a.lds = k / 16;
-  a.out_stride = n / hc; a.out_dtype = FP4X_BF16; a.post = 1.f; a.group = 16;
-  a.hc = (int)hc; a.bj = (int)bj; a.nrm = nrm; a.nrm_stride = nrm_stride;
-  fill_args(pl, a);
-  cudaStream_t st = (cudaStream_t)stream;
-  return RG == 1 ? launch_nt<FMT_W8, EPI_HC_UP, 1>(pl, a, 1, st) : launch_nt<FMT_W8, EPI_HC_UP, 2>(pl, a, 1, st);
+  return run_gemv(FMT_W8, x, x_stride, q, nullptr, s, 1.f, 16, di, bot, n, FP4X_BF16, m, n, k, ws, ws_bytes, counters,
+                  n_counters, stream, EPI_HC_DOWN, kStreamK, (int)lr, (int)hc);
 }
 
 int fp4x_hc_up(const void* bot, int64_t bot_stride, const void* qi, const void* si, const void* nrm,
                int64_t nrm_stride, void* out, int64_t m, int64_t n, int64_t k, int64_t hc, int64_t bj, void* stream) {
-  return hc_up_impl(bot, bot_stride, qi, si, nrm, nrm_stride, out, m, n, k, hc, bj, stream);
+  int rc;
+  if (!out || !nrm || !si) return fail(FP4X_ERR_INVALID_ARG, "null pointer");
+  if (hc < 1 || hc > 8 || bj < 1 || (hc * bj != 16 && hc * bj != 32) || n % (hc * bj) || n % kRB)
+    return fail(FP4X_ERR_UNSUPPORTED, "hc * bj must be 16 or 32 and the rows a multiple of 64");
+  Plan pl;
+  if ((rc = make_plan(FMT_W8, m, n, k, 1, 16, kWholeTile, 1, pl))) return rc;
+  if ((rc = check_x(bot, bot_stride, k))) return rc;
+  if ((rc = check_rows(qi, k, "weight"))) return rc;
+  const int scw = scale_width(si, k / 16, pl.SB);
+  if (!scw) return fail(FP4X_ERR_UNSUPPORTED, "scale rows must be 4-byte aligned");
+  GemvArgs a;
+  std::memset(&a, 0, sizeof(a));
+  if ((rc = encode_rows(&a.tm0, qi, n, k, pl.BI0))) return rc;
+  a.item = GemvItem{bot, (const uint8_t*)si, out, nullptr};
+  a.M = (int)m; a.N = (int)n; a.K = (int)k;
+  a.x_stride = bot_stride; a.lds = k / 16; a.scw = scw;
+  a.out_stride = n / hc; a.out_dtype = FP4X_BF16; a.post = 1.f; a.group = 16;
+  a.hc = (int)hc; a.bj = (int)bj; a.nrm = nrm; a.nrm_stride = nrm_stride;
+  fill_args(pl, a);
+  return launch_nt<FMT_W8, EPI_HC_UP>(pl, a, 1, (cudaStream_t)stream);
 }
 
 int fp4x_hc_mixer_unfused(const void* x, int64_t x_stride, const void* qd, const void* sd, const void* qu,
@@ -484,17 +611,16 @@ int fp4x_hc_mixer_unfused(const void* x, int64_t x_stride, const void* qd, const
   if (!di || !bot || !g || !out) return fail(FP4X_ERR_INVALID_ARG, "null output");
   if (lr < 1 || lr > n_down || hc < 1 || hc > 8 || n_up % hc) return fail(FP4X_ERR_INVALID_ARG, "bad lr/hc/n_up");
   cudaStream_t st = (cudaStream_t)stream;
-  // 1. down GEMV with the same plan as the fused kernel; epilogue writes only di (the cast)
-  if ((rc = run_gemv(FMT_W8, x, x_stride, qd, nullptr, sd, 1.f, 16, di, nullptr, n_down, FP4X_BF16, m, n_down, k,
-                     ws, ws_bytes, counters, n_counters, stream, EPI_HC_DOWN)))
+  // 1. down GEMV with the same plan as the fused kernel; its epilogue writes only di (the cast)
+  if ((rc = run_gemv(FMT_W8, x, x_stride, qd, nullptr, sd, 1.f, 16, di, nullptr, n_down, FP4X_BF16, m, n_down, k, ws,
+                     ws_bytes, counters, n_counters, stream, EPI_HC_DOWN, kStreamK, (int)lr, (int)hc)))
     return rc;
-  // (run_gemv's HC_DOWN epilogue takes lr/hc from the args; with bot == nullptr only di is stored)
   // 2. scaled SiLU
   if ((rc = check_launch(launch_pdl(hc_scaled_silu_kernel, dim3(64), dim3(256), 0, st, (const __nv_bfloat16*)di,
                                     (__nv_bfloat16*)bot, (int)m, (int)n_down, (int)lr, (int)hc),
                          "scaled silu")))
     return rc;
-  // 3. up GEMV on the original rows, whole-tile plan (same per-row arithmetic as the fused up kernel)
+  // 3. up GEMV on the original rows, whole-block plan (the same per-row arithmetic as the fused up kernel)
   if ((rc = run_gemv(FMT_W8, bot, lr, qu, nullptr, su, 1.f, 16, g, nullptr, n_up, FP4X_BF16, m, n_up, lr, nullptr, 0,
                      nullptr, 0, stream, EPI_STORE, kWholeTile)))
     return rc;

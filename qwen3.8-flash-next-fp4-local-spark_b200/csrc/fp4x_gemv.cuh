@@ -2,30 +2,34 @@
 //
 //   out[m, n] = sum_k x[m, k] * W[n, k]      x: bf16 [M, K];  W: packed rows in one of six formats
 //
-// Structure (one CTA per SM, 8 warps):
-//   * Work = (row tile of RU = 16*RG rows) x (k chunk of KC elements) "chunk units".  The K axis is cut into KP
-//     panels (grid.y); inside a panel the RT*NCH chunk units are split evenly across all CPP*8 warps of the
-//     panel (stream-K), so every warp streams the same number of bytes.
-//   * Each warp owns a ring of NS shared-memory stages.  Lanes issue one cp.async.bulk per weight row segment
-//     (codes) plus 4-byte cp.async for the scale words; an mbarrier per stage completes on the transaction
-//     bytes and the 32 async arrivals.  The first NS stages are issued before griddepcontrol.wait (weights
-//     never depend on the previous kernel).
-//   * The panel's activations are staged once per CTA in shared memory, already permuted into the mma B
-//     fragment order of the format and converted to f16 with a per-(token, panel) power-of-two scale (exact for
-//     every element within 2^31 of the token's panel maximum) or kept as bf16.
-//   * Weights are decoded in registers straight into m16n8k16 A fragments with exact conversions
-//     (fp8/fp4 -> f16 cvt, int8/int6 -> f16 magic-number adds, INT2 -> bf16 via a per-group byte-permute table)
-//     and multiplied on the tensor cores with fp32 accumulation.  Per-group scales are applied to the fp32
-//     group partials (deferred), so products stay exact.
-//   * A row tile split across warps or panels is combined by the last arriving warp, which sums the partial
-//     slots in a fixed order (deterministic) and runs the epilogue; the arrival counter is reset to zero.
+// Structure (up to two CTAs per SM; each CTA = 4 consumer warps + 1 producer warp):
+//   * Work unit = (block of 64 weight rows) x (k chunk of KC elements).  K is cut into KP panels (grid.y); inside a
+//     panel the RT*NCH units are split evenly over the CPP CTAs of the panel (stream-K), so every CTA streams the
+//     same number of bytes.  A row block shared by several CTAs or panels is combined by the last arriving warp,
+//     which sums the partial slots in a fixed order (deterministic) and resets its arrival counter to zero.
+//   * The producer warp streams each unit into a ring of shared-memory stages with 2D TMA loads
+//     (cp.async.bulk.tensor, box = {64 or 128 bytes, 64 rows}, 64B/128B swizzle: one 4-8 KB request per box),
+//     plus 16/8/4-byte cp.async copies of the scale rows.  It starts before griddepcontrol.wait: weights never
+//     depend on the previous kernel, so under programmatic dependent launch the first stages are already in
+//     flight while the previous kernel drains.
+//   * The panel's activations are staged once per CTA in shared memory, permuted into the mma B-fragment order of
+//     the format and converted to f16 with a per-(token, panel) power-of-two scale (exact for every element within
+//     2^31 of the token's panel maximum) or kept as bf16.
+//   * Each consumer warp owns 16 rows of the stage.  A fragments come straight from the swizzled tiles with
+//     ldmatrix (bank-conflict free), are decoded in registers with exact conversions (fp8/fp4 -> f16 cvt, int8/
+//     int6 -> f16 magic-number adds, INT2 -> bf16 via a per-group byte-permute table) and multiplied on the tensor
+//     cores (mma.sync m16n8k16, fp32 accumulate).  Per-group scales are applied to the fp32 group partials
+//     (deferred) for the fp8/int formats, so products stay exact.
 #pragma once
+#include <cuda.h>
+
 #include "fp4x_common.cuh"
 
 namespace fp4x {
 
-constexpr int kWarps = 8;
-constexpr int kThreads = kWarps * 32;
+constexpr int kCWarps = 4;                       // consumer warps
+constexpr int kThreads = (kCWarps + 1) * 32;     // + one producer warp
+constexpr int kRB = 16 * kCWarps;                // rows per stage
 constexpr int kMaxStages = 8;
 
 enum Fmt : int { FMT_MX8 = 0, FMT_W8 = 1, FMT_W6 = 2, FMT_NV4 = 3, FMT_BF16 = 4, FMT_INT2 = 5 };
@@ -33,58 +37,73 @@ enum Epi : int { EPI_STORE = 0, EPI_HC_DOWN = 1, EPI_HC_UP = 2, EPI_HEAD = 3 };
 
 // per-format geometry; bytes-per-k values are num/den
 struct FmtGeom {
-  int blk;        // k per decode block
+  int kq;         // k per 16-byte chunk of plane 0
   int n0, d0;     // plane-0 bytes per k
   int n1, d1;     // plane-1 bytes per k (0 if absent)
   int sn, sd;     // scale bytes per k (INT2: sd = group / 2)
   int qb;         // activation staging block (consecutive k)
   int xf16;       // activations converted to scaled f16 (else kept bf16)
-  int mod0, mod1; // shared-memory pitch residues mod 128 (bank-conflict-free reads)
+  int kmin;       // k granularity of a stage (one decode block of 64 or 128 plane-0 bytes)
 };
 
 __host__ __device__ constexpr FmtGeom fmt_geom(int fmt) {
-  return fmt == FMT_MX8    ? FmtGeom{32, 1, 1, 0, 1, 1, 32, 4, 1, 32, 0}
-         : fmt == FMT_W8   ? FmtGeom{64, 1, 1, 0, 1, 1, 16, 4, 1, 64, 0}
-         : fmt == FMT_W6   ? FmtGeom{32, 1, 2, 1, 4, 1, 16, 8, 1, 16, 16}
-         : fmt == FMT_NV4  ? FmtGeom{128, 1, 2, 0, 1, 1, 16, 4, 1, 64, 0}
-         : fmt == FMT_BF16 ? FmtGeom{32, 2, 1, 0, 1, 0, 1, 4, 0, 64, 0}
-                           : FmtGeom{256, 1, 4, 0, 1, 1, 8, 16, 0, 64, 0};  // INT2 (scale sd set at runtime)
+  return fmt == FMT_MX8    ? FmtGeom{16, 1, 1, 0, 1, 1, 32, 4, 1, 64}
+         : fmt == FMT_W8   ? FmtGeom{16, 1, 1, 0, 1, 1, 16, 4, 1, 64}
+         : fmt == FMT_W6   ? FmtGeom{32, 1, 2, 1, 4, 1, 16, 8, 1, 256}
+         : fmt == FMT_NV4  ? FmtGeom{32, 1, 2, 0, 1, 1, 16, 4, 1, 128}
+         : fmt == FMT_BF16 ? FmtGeom{8, 2, 1, 0, 1, 0, 1, 16, 0, 32}
+                           : FmtGeom{64, 1, 4, 0, 1, 1, 8, 16, 0, 256};  // INT2 (scale sd set at runtime)
 }
 
 struct GemvItem {
   const void* x;        // bf16 [M, K] (row stride x_stride elements)
-  const uint8_t* p0;    // code plane 0
-  const uint8_t* p1;    // code plane 1 (W6 high bits)
   const uint8_t* sc;    // scales
   void* out;            // primary output
   void* out2;           // HC down: bottleneck output; head: bf16 copy of the logits
 };
 
-struct GemvArgs {
+// one entry of a batched launch: the TMA descriptor of the codes plus the pointers of the item
+struct alignas(64) BatchEntry {
+  CUtensorMap tm0;
+  const void* x;
+  const uint8_t* sc;
+  void* out;
+  void* pad;
+};
+
+struct alignas(64) GemvArgs {
+  CUtensorMap tm0;        // plane-0 codes [N, ld0] uint8, box {BI0, 64}
+  CUtensorMap tm1;        // plane-1 codes (W6 high bit pairs), box {BI1, 64}
   GemvItem item;          // the matrix of a single call
-  const void* const* items4;  // batched W8: device array of {x, codes, scales, out} per grid.z, or null
+  const BatchEntry* batch;  // batched W8: one entry per grid.z (device memory), or null
   int M, N, K;
   int64_t x_stride;
-  int64_t ld0, ld1, lds;  // row strides (bytes)
+  int64_t lds;            // scale row stride (bytes)
   int64_t out_stride;     // elements between tokens of out (and out2 for the head)
   int out_dtype;
   float post;             // multiplier on the final sum (NVFP4 global scale)
   int KPW, KP;            // panel width and count
-  int KC, NCH;            // chunk width and chunks per (row tile, panel)
+  int KC, NCH;            // chunk width (k) and chunks per (row block, panel)
   int CPP;                // CTAs per (panel, batch item)
-  int RT;                 // row tiles
-  int NS;                 // stages per warp
-  int SMAX;               // partial slots per (batch, panel, row tile) when KP > 1
-  int whole;              // 1: warps own whole row tiles (all NCH chunks); no cross-warp reduction
+  int RT;                 // row blocks
+  int NS;                 // stages
+  int SMAX;               // partial slots per (batch, panel, row block) when KP > 1
+  int whole;              // 1: CTAs own whole row blocks (all NCH chunks)
   int group;              // INT2 scale group (16 or 32)
-  int P0, P1, PS, STG;    // stage pitches and stage bytes
+  int BI0, BI1;           // TMA box inner bytes of the planes (64 or 128)
+  int NB0;                // plane-0 boxes per stage
+  int SB;                 // scale bytes per row per stage
+  int scw;                // scale copy width (4, 8 or 16 bytes)
+  int STG;                // stage bytes (multiple of 1024)
+  int off_p1, off_sc;     // offsets of plane 1 and of the scales inside a stage
   int XP;                 // activation token pitch (bytes)
-  int smem_x, smem_stage, smem_scr;  // byte offsets of the shared-memory regions
+  int smem_x, smem_misc, smem_scr;  // offsets of the regions after the 1024-aligned base (stages start at 0)
+  int smem_xraw;          // raw bf16 activation panel [M][KPW] (bulk-copied after griddepcontrol.wait)
   int lr, hc, bj;         // hyper-connection epilogues
   const void* nrm;        // HC up: normalized input [M, hc*H]
   int64_t nrm_stride;
   float* ws;              // partial slots
-  int* sem;               // arrival counters [batch * RT], zero on entry and on exit
+  int* sem;               // arrival counters [batch * RT * 4], zero on entry and on exit
   int* err;               // device error word
 };
 
@@ -92,34 +111,70 @@ struct GemvArgs {
 // work partition helpers (identical on host and device)
 // ------------------------------------------------------------------------------------------------------
 __host__ __device__ inline int64_t range_begin(int64_t U, int W, int w) { return U * w / W; }
-// warp that owns chunk unit u when U units are split over W warps by range_begin
+// the part that owns unit u when U units are split over W parts by range_begin
 __host__ __device__ inline int owner_of(int64_t u, int64_t U, int W) { return (int)(((u + 1) * W + U - 1) / U) - 1; }
+
+// ------------------------------------------------------------------------------------------------------
+// TMA, async copies, ldmatrix
+// ------------------------------------------------------------------------------------------------------
+FP4X_DEV void tma_load_2d(uint32_t dst, const CUtensorMap* tm, int x, int y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          dst),
+      "l"(tm), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+FP4X_DEV void cp_async8(uint32_t dst, const void* src) {
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(dst), "l"(src) : "memory");
+}
+FP4X_DEV void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+FP4X_DEV void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+FP4X_DEV void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+FP4X_DEV void named_bar(int id, int threads) { asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory"); }
+
+// physical offset of logical byte `off` inside a tile written by TMA with the 64B/128B swizzle of box inner BI
+FP4X_DEV uint32_t swz(uint32_t off, int BI) {
+  const uint32_t mask = BI == 128 ? 7u : 3u;
+  return off ^ (((off >> 7) & mask) << 4);
+}
 
 // ------------------------------------------------------------------------------------------------------
 // activation staging: permuted B-fragment order, one quad (4 k values) per (token, step, tq)
 // ------------------------------------------------------------------------------------------------------
+// For a staging block kb (qb consecutive k of the panel) of format FMT: the steps of its quads and the tq.
 template <int FMT>
 FP4X_DEV void stage_block_positions(int kb, int (&s)[4], int& tq) {
-  if (FMT == FMT_MX8 || FMT == FMT_BF16) {  // k0 = 32j + 8tq + 4h
+  if (FMT == FMT_MX8) {  // k0 = 32G + 16h + 4tq
+    s[0] = 2 * (kb >> 3) + ((kb >> 2) & 1);
+    tq = kb & 3;
+  } else if (FMT == FMT_W8) {  // k0 = 64G + 16h + 4tq
+    s[0] = 4 * (kb >> 4) + ((kb >> 2) & 3);
+    tq = kb & 3;
+  } else if (FMT == FMT_NV4) {  // k0 = 32C + 8tq + 4h
     s[0] = 2 * (kb >> 3) + (kb & 1);
     tq = (kb >> 1) & 3;
-  } else if (FMT == FMT_W8) {  // k0 = 64j + 16tq + 4h
-    s[0] = 4 * (kb >> 4) + (kb & 3);
-    tq = (kb >> 2) & 3;
-  } else if (FMT == FMT_NV4) {  // k0 = 128b + 32tq + 4i
-    s[0] = 8 * (kb >> 5) + (kb & 7);
-    tq = (kb >> 3) & 3;
-  } else if (FMT == FMT_W6) {  // k0 = 32j + 8tq, two quads
+  } else if (FMT == FMT_W6) {  // k0 = 32G + 8tq: two quads
     s[0] = 2 * (kb >> 2);
     s[1] = s[0] + 1;
     tq = kb & 3;
-  } else {  // INT2: k0 = 256b + 64tq + 16gi, four quads
-    const int base = 16 * (kb >> 4) + 4 * (kb & 3);
+  } else if (FMT == FMT_BF16) {  // one 16-k step: four quads, one per tq
+    s[0] = kb;
+    tq = 0;
+  } else {  // INT2: one 16-k group kb = 4C + tq: four quads (steps 4C + p)
+    const int base = 4 * (kb >> 2);
     s[0] = base;
     s[1] = base + 1;
     s[2] = base + 2;
     s[3] = base + 3;
-    tq = (kb >> 2) & 3;
+    tq = kb & 3;
   }
 }
 
@@ -129,28 +184,39 @@ FP4X_DEV uint32_t cvt_pair(uint32_t bf2, float scl, bool xf16) {
   const float hi = bf16_bits_to_f32(bf2 >> 16) * scl;
   return pack_f16x2(lo, hi);
 }
+// two 16-bit values (halves lo_idx of lo_src and hi_idx of hi_src) in one word
 FP4X_DEV uint32_t pick2(uint32_t lo_src, int lo_idx, uint32_t hi_src, int hi_idx) {
-  // gather two 16-bit values (selected halves of two words) into one word
   const uint32_t a = (lo_src >> (16 * lo_idx)) & 0xffffu;
   const uint32_t b = (hi_src >> (16 * hi_idx)) & 0xffffu;
   return a | (b << 16);
 }
 
 template <int FMT>
-FP4X_DEV void stage_activations(const GemvArgs& A, const GemvItem& it, uint8_t* smem, int MP, int k_panel0) {
+FP4X_DEV void stage_activations(const GemvArgs& A, const GemvItem& it, uint8_t* base, int MP, int k_panel0,
+                                uint32_t xbar) {
   constexpr FmtGeom G = fmt_geom(FMT);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  float* xsc = reinterpret_cast<float*>(smem + kWarps * kMaxStages * 8);  // [MP] scale, [MP] inverse
-  const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(it.x);
+  constexpr int nthr = kCWarps * 32;
+  float* xsc = reinterpret_cast<float*>(base + A.smem_misc);  // [MP] scale, [MP] inverse
   const int KPW = A.KPW;
+  // one bulk copy per token row brings the raw panel into shared memory in a single round trip
+  const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(base + A.smem_xraw);
+  if (tid == 0) {
+    const uint32_t bytes = (uint32_t)KPW * 2u;
+    mbar_arrive_expect_tx(xbar, bytes * (uint32_t)A.M);
+    const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(it.x);
+    for (int m = 0; m < A.M; ++m)
+      bulk_g2s(smem_u32(base + A.smem_xraw) + m * bytes, x + (int64_t)m * A.x_stride + k_panel0, bytes, xbar);
+  }
+  if (!mbar_wait_bounded(xbar, 0, A.err)) return;
   if (G.xf16) {
-    for (int tok = warp; tok < MP; tok += kWarps) {
+    for (int tok = warp; tok < MP; tok += kCWarps) {
       float mx = 0.f;
       if (tok < A.M) {
-        const uint4* row = reinterpret_cast<const uint4*>(x + (int64_t)tok * A.x_stride + k_panel0);
+        const uint4* row = reinterpret_cast<const uint4*>(xr + (int64_t)tok * KPW);
         for (int i = lane; i < KPW / 8; i += 32) {
-          uint4 v = __ldg(row + i);
-          uint32_t w[4] = {v.x, v.y, v.z, v.w};
+          const uint4 v = row[i];
+          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             mx = fmaxf(mx, fabsf(bf16_bits_to_f32(w[e] & 0xffffu)));
@@ -172,25 +238,25 @@ FP4X_DEV void stage_activations(const GemvArgs& A, const GemvItem& it, uint8_t* 
         xsc[MP + tok] = __uint_as_float((uint32_t)(127 - t) << 23);
       }
     }
-    __syncthreads();
+    named_bar(1, nthr);
   }
-  const uint32_t xbase = smem_u32(smem + A.smem_x);
+  const uint32_t xbase = smem_u32(base + A.smem_x);
   const int nblk = KPW / G.qb;
-  for (int idx = tid; idx < MP * nblk; idx += kThreads) {
+  for (int idx = tid; idx < MP * nblk; idx += nthr) {
     const int tok = idx / nblk, kb = idx - tok * nblk;
     const float scl = G.xf16 ? xsc[tok] : 1.f;
     uint32_t v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
     if (tok < A.M) {
-      const __nv_bfloat16* src = x + (int64_t)tok * A.x_stride + k_panel0 + kb * G.qb;
+      const __nv_bfloat16* src = xr + (int64_t)tok * KPW + kb * G.qb;
       if (G.qb == 4) {
-        uint2 t = *reinterpret_cast<const uint2*>(src);
+        const uint2 t = *reinterpret_cast<const uint2*>(src);
         v[0] = t.x; v[1] = t.y;
       } else if (G.qb == 8) {
-        uint4 t = *reinterpret_cast<const uint4*>(src);
+        const uint4 t = *reinterpret_cast<const uint4*>(src);
         v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
       } else {
-        uint4 t0 = *reinterpret_cast<const uint4*>(src);
-        uint4 t1 = *reinterpret_cast<const uint4*>(src + 8);
+        const uint4 t0 = *reinterpret_cast<const uint4*>(src);
+        const uint4 t1 = *reinterpret_cast<const uint4*>(src + 8);
         v[0] = t0.x; v[1] = t0.y; v[2] = t0.z; v[3] = t0.w;
         v[4] = t1.x; v[5] = t1.y; v[6] = t1.z; v[7] = t1.w;
       }
@@ -198,159 +264,187 @@ FP4X_DEV void stage_activations(const GemvArgs& A, const GemvItem& it, uint8_t* 
     int s[4];
     int tq;
     stage_block_positions<FMT>(kb, s, tq);
-    const uint32_t trow = xbase + tok * A.XP + tq * 8;
+    const uint32_t trow = xbase + tok * A.XP;
     if (G.qb == 4) {
-      sts64(trow + s[0] * 32, cvt_pair(v[0], scl, G.xf16), cvt_pair(v[1], scl, G.xf16));
+      sts64(trow + s[0] * 32 + tq * 8, cvt_pair(v[0], scl, G.xf16), cvt_pair(v[1], scl, G.xf16));
     } else if (G.qb == 8) {
-      // elements r0..r7 in v[0..3] (two per word); quads (r0,r4,r1,r5) and (r2,r6,r3,r7)
-      sts64(trow + s[0] * 32, cvt_pair(pick2(v[0], 0, v[2], 0), scl, G.xf16),
+      // W6: elements r0..r7 (two per word); quads (r0,r4,r1,r5) and (r2,r6,r3,r7)
+      sts64(trow + s[0] * 32 + tq * 8, cvt_pair(pick2(v[0], 0, v[2], 0), scl, G.xf16),
             cvt_pair(pick2(v[0], 1, v[2], 1), scl, G.xf16));
-      sts64(trow + s[1] * 32, cvt_pair(pick2(v[1], 0, v[3], 0), scl, G.xf16),
+      sts64(trow + s[1] * 32 + tq * 8, cvt_pair(pick2(v[1], 0, v[3], 0), scl, G.xf16),
             cvt_pair(pick2(v[1], 1, v[3], 1), scl, G.xf16));
+    } else if (FMT == FMT_BF16) {
+      // one step of 16 k: quad q = (e[2q], e[2q+1], e[8+2q], e[9+2q]) = words v[q], v[4+q]
+#pragma unroll
+      for (int q = 0; q < 4; ++q) sts64(trow + s[0] * 32 + q * 8, v[q], v[4 + q]);
     } else {
-      // elements e0..e15 in v[0..7]; quad p = (ORDER[p], 4+ORDER[p], 8+ORDER[p], 12+ORDER[p]), ORDER=(0,2,1,3)
+      // INT2: elements e0..e15 of one group; quad p = (ORDER[p] + 4j), ORDER = (0,2,1,3)
 #pragma unroll
       for (int p = 0; p < 4; ++p) {
         const int o = (p == 1) ? 2 : (p == 2 ? 1 : p);
-        // element e lives in v[e/2], half e%2
         const int e0 = o, e1 = 4 + o, e2 = 8 + o, e3 = 12 + o;
         const uint32_t lo = pick2(v[e0 >> 1], e0 & 1, v[e1 >> 1], e1 & 1);
         const uint32_t hi = pick2(v[e2 >> 1], e2 & 1, v[e3 >> 1], e3 & 1);
-        sts64(trow + s[p] * 32, cvt_pair(lo, scl, G.xf16), cvt_pair(hi, scl, G.xf16));
+        sts64(trow + s[p] * 32 + tq * 8, cvt_pair(lo, scl, G.xf16), cvt_pair(hi, scl, G.xf16));
       }
     }
   }
 }
 
 // ------------------------------------------------------------------------------------------------------
-// per-format chunk compute: accumulate one (RU rows x KC) chunk into acc
+// per-format stage compute: one warp, 16 rows, one stage
 // ------------------------------------------------------------------------------------------------------
-struct ChunkCtx {
-  uint32_t a0, a1, sc;  // shared addresses of the stage planes and scales
-  int P0, P1, PS;
-  int KC;
-  uint32_t xb;          // shared address of the activation tile for step 0 of this chunk, token row g, tq
+struct WarpCtx {
+  uint32_t p0, p1, sc;  // shared addresses of the stage planes and scales
+  int BI0, BI1, NB0, SB;
+  uint32_t lrow0;       // ldmatrix: this lane's row offset inside a box (row * BI0)
+  int lswz, lsel;       // ldmatrix: this lane's swizzle key and chunk select (0/1)
+  uint32_t xb;          // activation address of step 0 of this stage for token row g and tq
   int XP;
-  int g, tq;
-  int group;            // INT2 scale group
+  int g, tq, rbase;     // rbase = 16 * warp (first row of the warp inside the stage)
+  int gshift;           // INT2: 1 when scale groups are 32
 };
 
 template <int NT>
-FP4X_DEV void load_b(const ChunkCtx& c, int s, uint32_t (&b0)[NT], uint32_t (&b1)[NT]) {
+FP4X_DEV void load_b(const WarpCtx& c, int s, uint32_t (&b0)[NT], uint32_t (&b1)[NT]) {
 #pragma unroll
   for (int t = 0; t < NT; ++t) {
-    uint2 v = lds64(c.xb + t * 8 * c.XP + s * 32);
+    const uint2 v = lds64(c.xb + t * 8 * c.XP + s * 32);
     b0[t] = v.x;
     b1[t] = v.y;
   }
 }
 
-template <int NT, int RG>
-FP4X_DEV void zero_acc(float (&a)[RG][NT][4]) {
-#pragma unroll
-  for (int r = 0; r < RG; ++r)
-#pragma unroll
-    for (int t = 0; t < NT; ++t)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) a[r][t][e] = 0.f;
+// chunks (chunk, chunk+1) x (rows g, g+8) of plane 0, box b: r0 = (g, chunk), r1 = (g+8, chunk),
+// r2 = (g, chunk+1), r3 = (g+8, chunk+1); each register = bytes 4tq..4tq+3 of that 16-byte row chunk
+FP4X_DEV void ld_pair(const WarpCtx& c, int b, int chunk, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  const uint32_t addr =
+      c.p0 + (uint32_t)b * (uint32_t)(kRB * c.BI0) + c.lrow0 + 16u * (uint32_t)((chunk + c.lsel) ^ c.lswz);
+  ldsm_x4(addr, r0, r1, r2, r3);
 }
 
-template <int NT, int RG>
-FP4X_DEV void fma_scaled(float (&acc)[RG][NT][4], const float (&tmp)[RG][NT][4], const float (&s_lo)[RG],
-                         const float (&s_hi)[RG]) {
+template <int NT>
+FP4X_DEV void zero4(float (&a)[NT][4]) {
 #pragma unroll
-  for (int r = 0; r < RG; ++r)
+  for (int t = 0; t < NT; ++t)
 #pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      acc[r][t][0] = fmaf(tmp[r][t][0], s_lo[r], acc[r][t][0]);
-      acc[r][t][1] = fmaf(tmp[r][t][1], s_lo[r], acc[r][t][1]);
-      acc[r][t][2] = fmaf(tmp[r][t][2], s_hi[r], acc[r][t][2]);
-      acc[r][t][3] = fmaf(tmp[r][t][3], s_hi[r], acc[r][t][3]);
-    }
+    for (int e = 0; e < 4; ++e) a[t][e] = 0.f;
 }
 
-template <int NT, int RG>
-FP4X_DEV void chunk_mx8(const ChunkCtx& c, float (&acc)[RG][NT][4]) {
-  const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-  for (int j = 0; j < c.KC / 32; ++j) {
-    uint2 a[RG][2];
+template <int NT>
+FP4X_DEV void fma_scaled(float (&acc)[NT][4], const float (&tmp)[NT][4], float s_lo, float s_hi) {
 #pragma unroll
-    for (int r = 0; r < RG; ++r) {
-      const int row = 16 * r + c.g;
-      a[r][0] = lds64(c.a0 + row * c.P0 + 32 * j + 8 * c.tq);
-      a[r][1] = lds64(c.a0 + (row + 8) * c.P0 + 32 * j + 8 * c.tq);
-    }
-    float tmp[RG][NT][4];
-#pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint32_t b0[NT], b1[NT];
-      load_b<NT>(c, 2 * j + h, b0, b1);
-#pragma unroll
-      for (int r = 0; r < RG; ++r) {
-        const uint32_t w0 = h ? a[r][0].y : a[r][0].x;
-        const uint32_t w1 = h ? a[r][1].y : a[r][1].x;
-        const uint32_t A[4] = {e4m3x2_to_f16x2(w0), e4m3x2_to_f16x2(w1), e4m3x2_to_f16x2(w0 >> 16),
-                               e4m3x2_to_f16x2(w1 >> 16)};
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          if (h == 0)
-            mma_f16(tmp[r][t], A, b0[t], b1[t], zero);
-          else
-            mma_f16(tmp[r][t], A, b0[t], b1[t], tmp[r][t]);
-        }
-      }
-    }
-    float sl[RG], sh[RG];
-#pragma unroll
-    for (int r = 0; r < RG; ++r) {
-      const int row = 16 * r + c.g;
-      sl[r] = e8m0_to_f32(lds8(c.sc + row * c.PS + j));
-      sh[r] = e8m0_to_f32(lds8(c.sc + (row + 8) * c.PS + j));
-    }
-    fma_scaled<NT, RG>(acc, tmp, sl, sh);
+  for (int t = 0; t < NT; ++t) {
+    acc[t][0] = fmaf(tmp[t][0], s_lo, acc[t][0]);
+    acc[t][1] = fmaf(tmp[t][1], s_lo, acc[t][1]);
+    acc[t][2] = fmaf(tmp[t][2], s_hi, acc[t][2]);
+    acc[t][3] = fmaf(tmp[t][3], s_hi, acc[t][3]);
   }
 }
 
-template <int NT, int RG>
-FP4X_DEV void chunk_w8(const ChunkCtx& c, float (&acc)[RG][NT][4]) {
-  const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-  const uint32_t kMagic = 0x64646464u, kNeg1152 = 0xE480E480u;
-  for (int j = 0; j < c.KC / 64; ++j) {
-    uint4 a[RG][2];
+template <int NT>
+FP4X_DEV void mma_f16_acc(float (&d)[NT][4], const uint32_t (&a)[4], const uint32_t (&b0)[NT],
+                          const uint32_t (&b1)[NT], bool fresh) {
+  const float z[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-    for (int r = 0; r < RG; ++r) {
-      const int row = 16 * r + c.g;
-      a[r][0] = lds128(c.a0 + row * c.P0 + 64 * j + 16 * c.tq);
-      a[r][1] = lds128(c.a0 + (row + 8) * c.P0 + 64 * j + 16 * c.tq);
+  for (int t = 0; t < NT; ++t) {
+    if (fresh) mma_f16(d[t], a, b0[t], b1[t], z);
+    else mma_f16(d[t], a, b0[t], b1[t], d[t]);
+  }
+}
+template <int NT>
+FP4X_DEV void mma_bf16_acc(float (&d)[NT][4], const uint32_t (&a)[4], const uint32_t (&b0)[NT],
+                           const uint32_t (&b1)[NT]) {
+#pragma unroll
+  for (int t = 0; t < NT; ++t) mma_bf16(d[t], a, b0[t], b1[t], d[t]);
+}
+
+// The stage functions below are fully unrolled over a compile-time stage shape (CPB 16-byte chunks per box: 8 for
+// 128-byte boxes, 4 for 64-byte boxes; NB boxes per stage).  Every shared-memory load of a box (ldmatrix
+// fragments, activation fragments, scales) is issued before the arithmetic that consumes it, so the load latencies
+// overlap, and formats that chain MMAs spread them over independent accumulators.
+
+template <int NT, int NACC>
+FP4X_DEV void zero_accs(float (&a)[NACC][NT][4]) {
+#pragma unroll
+  for (int i = 0; i < NACC; ++i) zero4<NT>(a[i]);
+}
+template <int NT, int NACC>
+FP4X_DEV void fold_accs(float (&acc)[NT][4], const float (&a)[NACC][NT][4]) {
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      float v = a[0][t][e];
+#pragma unroll
+      for (int i = 1; i < NACC; ++i) v += a[i][t][e];
+      acc[t][e] += v;
     }
-    float tmp[RG][NT][4];
+}
+
+// MXFP8: a chunk pair is one 32-group G; steps 2G + h; group scales applied to the fp32 group sums
+template <int NT, int CPB, int NB>
+FP4X_DEV void stage_mx8(const WarpCtx& c, float (&acc)[NT][4]) {
+  constexpr int GPB = CPB / 2, NG = NB * GPB, NW = (NG + 3) / 4;
+  uint32_t r[NG][4];
+  uint32_t b0[2 * NG][NT], b1[2 * NG][NT];
+  uint32_t slo[NW], shi[NW];
+#pragma unroll
+  for (int j = 0; j < NG; ++j) ld_pair(c, j / GPB, 2 * (j % GPB), r[j][0], r[j][1], r[j][2], r[j][3]);
+#pragma unroll
+  for (int s = 0; s < 2 * NG; ++s) load_b<NT>(c, s, b0[s], b1[s]);
+#pragma unroll
+  for (int i = 0; i < NW; ++i) {
+    slo[i] = lds32(c.sc + (c.rbase + c.g) * c.SB + 4 * i);
+    shi[i] = lds32(c.sc + (c.rbase + c.g + 8) * c.SB + 4 * i);
+  }
+#pragma unroll
+  for (int j = 0; j < NG; ++j) {
+    float tmp[NT][4];
+    const uint32_t A0[4] = {e4m3x2_to_f16x2(r[j][0]), e4m3x2_to_f16x2(r[j][1]), e4m3x2_to_f16x2(r[j][0] >> 16),
+                            e4m3x2_to_f16x2(r[j][1] >> 16)};
+    mma_f16_acc<NT>(tmp, A0, b0[2 * j], b1[2 * j], true);
+    const uint32_t A1[4] = {e4m3x2_to_f16x2(r[j][2]), e4m3x2_to_f16x2(r[j][3]), e4m3x2_to_f16x2(r[j][2] >> 16),
+                            e4m3x2_to_f16x2(r[j][3] >> 16)};
+    mma_f16_acc<NT>(tmp, A1, b0[2 * j + 1], b1[2 * j + 1], false);
+    const float sl = e8m0_to_f32((slo[j >> 2] >> (8 * (j & 3))) & 0xffu);
+    const float sh = e8m0_to_f32((shi[j >> 2] >> (8 * (j & 3))) & 0xffu);
+    fma_scaled<NT>(acc, tmp, sl, sh);
+  }
+}
+
+FP4X_DEV uint32_t w8_pair_lo(uint32_t w) { return hadd2(prmt(w ^ 0x80808080u, 0x64646464u, 0x4140u), 0xE480E480u); }
+FP4X_DEV uint32_t w8_pair_hi(uint32_t w) { return hadd2(prmt(w ^ 0x80808080u, 0x64646464u, 0x4342u), 0xE480E480u); }
+
+// W8: four chunks per 64-group G; steps 4G + h
+template <int NT, int CPB, int NB>
+FP4X_DEV void stage_w8(const WarpCtx& c, float (&acc)[NT][4]) {
+  constexpr int GPB = CPB / 4, NG = NB * GPB;
+  uint32_t r[NG][8];
+  uint32_t b0[4 * NG][NT], b1[4 * NG][NT];
+  float slo[NG], shi[NG];
+#pragma unroll
+  for (int j = 0; j < NG; ++j) {
+    ld_pair(c, j / GPB, 4 * (j % GPB), r[j][0], r[j][1], r[j][2], r[j][3]);
+    ld_pair(c, j / GPB, 4 * (j % GPB) + 2, r[j][4], r[j][5], r[j][6], r[j][7]);
+  }
+#pragma unroll
+  for (int s = 0; s < 4 * NG; ++s) load_b<NT>(c, s, b0[s], b1[s]);
+#pragma unroll
+  for (int j = 0; j < NG; ++j) {
+    slo[j] = __uint_as_float(lds32(c.sc + (c.rbase + c.g) * c.SB + 4 * j));
+    shi[j] = __uint_as_float(lds32(c.sc + (c.rbase + c.g + 8) * c.SB + 4 * j));
+  }
+#pragma unroll
+  for (int j = 0; j < NG; ++j) {
+    float tmp[NT][4];
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
-      uint32_t b0[NT], b1[NT];
-      load_b<NT>(c, 4 * j + h, b0, b1);
-#pragma unroll
-      for (int r = 0; r < RG; ++r) {
-        const uint32_t w0 = (h == 0 ? a[r][0].x : h == 1 ? a[r][0].y : h == 2 ? a[r][0].z : a[r][0].w) ^ 0x80808080u;
-        const uint32_t w1 = (h == 0 ? a[r][1].x : h == 1 ? a[r][1].y : h == 2 ? a[r][1].z : a[r][1].w) ^ 0x80808080u;
-        const uint32_t A[4] = {hadd2(prmt(w0, kMagic, 0x4140u), kNeg1152), hadd2(prmt(w1, kMagic, 0x4140u), kNeg1152),
-                               hadd2(prmt(w0, kMagic, 0x4342u), kNeg1152), hadd2(prmt(w1, kMagic, 0x4342u), kNeg1152)};
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          if (h == 0)
-            mma_f16(tmp[r][t], A, b0[t], b1[t], zero);
-          else
-            mma_f16(tmp[r][t], A, b0[t], b1[t], tmp[r][t]);
-        }
-      }
+      const uint32_t lo = r[j][2 * h], hi = r[j][2 * h + 1];  // rows g, g+8 of chunk 4j + h
+      const uint32_t A[4] = {w8_pair_lo(lo), w8_pair_lo(hi), w8_pair_hi(lo), w8_pair_hi(hi)};
+      mma_f16_acc<NT>(tmp, A, b0[4 * j + h], b1[4 * j + h], h == 0);
     }
-    float sl[RG], sh[RG];
-#pragma unroll
-    for (int r = 0; r < RG; ++r) {
-      const int row = 16 * r + c.g;
-      sl[r] = __uint_as_float(lds32(c.sc + row * c.PS + 4 * j));
-      sh[r] = __uint_as_float(lds32(c.sc + (row + 8) * c.PS + 4 * j));
-    }
-    fma_scaled<NT, RG>(acc, tmp, sl, sh);
+    fma_scaled<NT>(acc, tmp, slo[j], shi[j]);
   }
 }
 
@@ -358,123 +452,124 @@ FP4X_DEV uint32_t w6_lane(uint32_t lo_src, uint32_t hi_src) {
   return (lo_src & 0x000F000Fu) | (hi_src & 0x00300030u) | 0x64006400u;
 }
 
-template <int NT, int RG>
-FP4X_DEV void chunk_w6(const ChunkCtx& c, float (&acc)[RG][NT][4]) {
-  const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+// W6: a chunk of the low-nibble plane is one 32-group G (thread: 8 k = 32G + 8tq + r); steps 2G + h.
+// Processed one box (CPB groups) at a time.
+template <int NT, int CPB, int NB>
+FP4X_DEV void stage_w6(const WarpCtx& c, float (&acc)[NT][4]) {
   const uint32_t kNeg1056 = 0xE420E420u;
-  for (int j = 0; j < c.KC / 32; ++j) {
-    uint32_t L[RG][2], Hs[RG][2];
 #pragma unroll
-    for (int r = 0; r < RG; ++r) {
+  for (int b = 0; b < NB; ++b) {
+    uint32_t r[CPB / 2][4];
+    uint32_t hs[CPB][2];
+    uint32_t b0[2 * CPB][NT], b1[2 * CPB][NT];
+    uint32_t sw[2][CPB / 2];
+#pragma unroll
+    for (int u = 0; u < CPB / 2; ++u) ld_pair(c, b, 2 * u, r[u][0], r[u][1], r[u][2], r[u][3]);
+#pragma unroll
+    for (int gg = 0; gg < CPB; ++gg) {
+      const int G = b * CPB + gg;
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
-        const int row = 16 * r + c.g + 8 * q;
-        L[r][q] = lds32(c.a0 + row * c.P0 + 16 * j + 4 * c.tq);
-        Hs[r][q] = prmt(lds16(c.a1 + row * c.P1 + 8 * j + 2 * c.tq), 0u, 0x4140u);
+        const int row = c.rbase + c.g + 8 * q;
+        hs[gg][q] = lds16(c.p1 + swz((uint32_t)(row * c.BI1 + 8 * G + 2 * c.tq), c.BI1));
       }
     }
-    float tmp[RG][NT][4];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint32_t b0[NT], b1[NT];
-      load_b<NT>(c, 2 * j + h, b0, b1);
+    for (int s = 0; s < 2 * CPB; ++s) load_b<NT>(c, 2 * b * CPB + s, b0[s], b1[s]);
 #pragma unroll
-      for (int r = 0; r < RG; ++r) {
+    for (int i = 0; i < CPB / 2; ++i) {
+      sw[0][i] = lds32(c.sc + (c.rbase + c.g) * c.SB + 2 * b * CPB + 4 * i);
+      sw[1][i] = lds32(c.sc + (c.rbase + c.g + 8) * c.SB + 2 * b * CPB + 4 * i);
+    }
+#pragma unroll
+    for (int gg = 0; gg < CPB; ++gg) {
+      uint32_t L[2], Hs[2];
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        L[q] = r[gg >> 1][2 * (gg & 1) + q];
+        Hs[q] = prmt(hs[gg][q], 0u, 0x4140u);
+      }
+      float tmp[NT][4];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
         uint32_t A[4];
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
           uint32_t lo, hi;
           if (h == 0) {
-            lo = w6_lane(L[r][q], Hs[r][q] << 4);          // elements r0, r4
-            hi = w6_lane(L[r][q] >> 4, Hs[r][q]);          // r1, r5
+            lo = w6_lane(L[q], Hs[q] << 4);         // elements r0, r4
+            hi = w6_lane(L[q] >> 4, Hs[q]);         // r1, r5
           } else {
-            lo = w6_lane(L[r][q] >> 8, Hs[r][q] << 2);     // r2, r6
-            hi = w6_lane(L[r][q] >> 12, Hs[r][q] >> 2);    // r3, r7
+            lo = w6_lane(L[q] >> 8, Hs[q] << 2);    // r2, r6
+            hi = w6_lane(L[q] >> 12, Hs[q] >> 2);   // r3, r7
           }
           A[q] = hadd2(lo, kNeg1056);
           A[2 + q] = hadd2(hi, kNeg1056);
         }
-#pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          if (h == 0)
-            mma_f16(tmp[r][t], A, b0[t], b1[t], zero);
-          else
-            mma_f16(tmp[r][t], A, b0[t], b1[t], tmp[r][t]);
-        }
+        mma_f16_acc<NT>(tmp, A, b0[2 * gg + h], b1[2 * gg + h], h == 0);
       }
-    }
-    float sl[RG], sh[RG];
-#pragma unroll
-    for (int r = 0; r < RG; ++r) {
-      const int row = 16 * r + c.g;
-      sl[r] = f16_bits_to_f32(lds16(c.sc + row * c.PS + 2 * j));
-      sh[r] = f16_bits_to_f32(lds16(c.sc + (row + 8) * c.PS + 2 * j));
-    }
-    fma_scaled<NT, RG>(acc, tmp, sl, sh);
-  }
-}
-
-template <int NT, int RG>
-FP4X_DEV void chunk_nv4(const ChunkCtx& c, float (&acc)[RG][NT][4]) {
-  for (int blk = 0; blk < c.KC / 128; ++blk) {
-    uint4 a[RG][2];
-    uint32_t sA[RG][2], sB[RG][2];
-#pragma unroll
-    for (int r = 0; r < RG; ++r) {
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const int row = 16 * r + c.g + 8 * q;
-        a[r][q] = lds128(c.a0 + row * c.P0 + 64 * blk + 16 * c.tq);
-        const uint32_t sf = e4m3x2_to_f16x2(lds16(c.sc + row * c.PS + 8 * blk + 2 * c.tq));
-        sA[r][q] = prmt(sf, 0u, 0x1010u);
-        sB[r][q] = prmt(sf, 0u, 0x3232u);
-      }
-    }
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      uint32_t b0[NT], b1[NT];
-      load_b<NT>(c, 8 * blk + i, b0, b1);
-#pragma unroll
-      for (int r = 0; r < RG; ++r) {
-        uint32_t A[4];
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const uint32_t wv = (i >> 1) == 0 ? a[r][q].x : (i >> 1) == 1 ? a[r][q].y : (i >> 1) == 2 ? a[r][q].z : a[r][q].w;
-          const uint32_t hw = (i & 1) ? (wv >> 16) : wv;
-          const uint32_t s2 = i < 4 ? sA[r][q] : sB[r][q];
-          A[q] = hmul2(e2m1x2_to_f16x2(hw), s2);
-          A[2 + q] = hmul2(e2m1x2_to_f16x2(hw >> 8), s2);
-        }
-#pragma unroll
-        for (int t = 0; t < NT; ++t) mma_f16(acc[r][t], A, b0[t], b1[t], acc[r][t]);
-      }
+      const float sl = f16_bits_to_f32((sw[0][gg >> 1] >> (16 * (gg & 1))) & 0xffffu);
+      const float sh = f16_bits_to_f32((sw[1][gg >> 1] >> (16 * (gg & 1))) & 0xffffu);
+      fma_scaled<NT>(acc, tmp, sl, sh);
     }
   }
 }
 
-template <int NT, int RG>
-FP4X_DEV void chunk_bf16(const ChunkCtx& c, float (&acc)[RG][NT][4]) {
-  for (int u = 0; u < c.KC / 32; ++u) {
-    uint4 a[RG][2];
+// NVFP4: a chunk C is 32 k = two 16-groups (thread: k = 32C + 8tq + 4h + i, group 2C + tq/2); steps 2C + h.
+// The e4m3 block scale multiplies the e2m1 values in f16 (exact: <= 6 significant bits, normal range).
+template <int NT, int CPB, int NB>
+FP4X_DEV void stage_nv4(const WarpCtx& c, float (&acc)[NT][4]) {
+  constexpr int NACC = 4;
 #pragma unroll
-    for (int r = 0; r < RG; ++r) {
-      const int row = 16 * r + c.g;
-      a[r][0] = lds128(c.a0 + row * c.P0 + 64 * u + 16 * c.tq);
-      a[r][1] = lds128(c.a0 + (row + 8) * c.P0 + 64 * u + 16 * c.tq);
+  for (int b = 0; b < NB; ++b) {
+    uint32_t r[CPB / 2][4];
+    uint32_t b0[2 * CPB][NT], b1[2 * CPB][NT];
+    uint32_t sc8[CPB][2];
+#pragma unroll
+    for (int u = 0; u < CPB / 2; ++u) ld_pair(c, b, 2 * u, r[u][0], r[u][1], r[u][2], r[u][3]);
+#pragma unroll
+    for (int s = 0; s < 2 * CPB; ++s) load_b<NT>(c, 2 * b * CPB + s, b0[s], b1[s]);
+#pragma unroll
+    for (int cc = 0; cc < CPB; ++cc) {
+      const int grp = 2 * (b * CPB + cc) + (c.tq >> 1);
+      sc8[cc][0] = lds8(c.sc + (c.rbase + c.g) * c.SB + grp);
+      sc8[cc][1] = lds8(c.sc + (c.rbase + c.g + 8) * c.SB + grp);
     }
+    float accs[NACC][NT][4];
+    zero_accs<NT, NACC>(accs);
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      uint32_t b0[NT], b1[NT];
-      load_b<NT>(c, 2 * u + h, b0, b1);
+    for (int cc = 0; cc < CPB; ++cc) {
+      const uint32_t s2lo = prmt(e4m3x2_to_f16x2(sc8[cc][0]), 0u, 0x1010u);
+      const uint32_t s2hi = prmt(e4m3x2_to_f16x2(sc8[cc][1]), 0u, 0x1010u);
+      const uint32_t wlo = r[cc >> 1][2 * (cc & 1)], whi = r[cc >> 1][2 * (cc & 1) + 1];
 #pragma unroll
-      for (int r = 0; r < RG; ++r) {
-        const uint32_t A[4] = {h ? a[r][0].z : a[r][0].x, h ? a[r][1].z : a[r][1].x, h ? a[r][0].w : a[r][0].y,
-                               h ? a[r][1].w : a[r][1].y};
-#pragma unroll
-        for (int t = 0; t < NT; ++t) mma_bf16(acc[r][t], A, b0[t], b1[t], acc[r][t]);
+      for (int h = 0; h < 2; ++h) {
+        const uint32_t A[4] = {hmul2(e2m1x2_to_f16x2(wlo >> (16 * h)), s2lo),
+                               hmul2(e2m1x2_to_f16x2(whi >> (16 * h)), s2hi),
+                               hmul2(e2m1x2_to_f16x2(wlo >> (16 * h + 8)), s2lo),
+                               hmul2(e2m1x2_to_f16x2(whi >> (16 * h + 8)), s2hi)};
+        mma_f16_acc<NT>(accs[(2 * cc + h) % NACC], A, b0[2 * cc + h], b1[2 * cc + h], false);
       }
     }
+    fold_accs<NT, NACC>(acc, accs);
   }
+}
+
+// BF16: a chunk pair is one standard 16-k step
+template <int NT, int CPB, int NB>
+FP4X_DEV void stage_bf16(const WarpCtx& c, float (&acc)[NT][4]) {
+  constexpr int SPB = CPB / 2, NS_ = NB * SPB, NACC = 2;
+  uint32_t A[NS_][4];
+  uint32_t b0[NS_][NT], b1[NS_][NT];
+#pragma unroll
+  for (int s = 0; s < NS_; ++s) ld_pair(c, s / SPB, 2 * (s % SPB), A[s][0], A[s][1], A[s][2], A[s][3]);
+#pragma unroll
+  for (int s = 0; s < NS_; ++s) load_b<NT>(c, s, b0[s], b1[s]);
+  float accs[NACC][NT][4];
+  zero_accs<NT, NACC>(accs);
+#pragma unroll
+  for (int s = 0; s < NS_; ++s) mma_bf16_acc<NT>(accs[s % NACC], A[s], b0[s], b1[s]);
+  fold_accs<NT, NACC>(acc, accs);
 }
 
 // INT2 group table: bytes T[c] (c = code) of bf16 values (-a, -b, +b, +a), a = bf16(1.5 s), b = bf16(0.5 s)
@@ -485,66 +580,80 @@ FP4X_DEV void int2_table(uint32_t s16, uint32_t& tlo, uint32_t& thi) {
   thi = prmt(pk, 0u, 0x3113u) ^ 0x00008080u;
 }
 
-template <int NT, int RG>
-FP4X_DEV void chunk_int2(const ChunkCtx& c, float (&acc)[RG][NT][4]) {
-  const int gshift = c.group == 32 ? 1 : 0;
-  for (int blk = 0; blk < c.KC / 256; ++blk) {
-    uint4 a[RG][2];
+// INT2: a chunk C is 64 k = four 16-groups; thread tq owns group 4C + tq; steps 4C + p.
+// Processed in 128-k units (two chunks, eight steps) to bound the registers held.  The four partial sums are folded
+// into `acc` after every unit, so a row's summation order depends on K alone and not on the stage shape the planner
+// picked: vocabulary shards of one head then give bit-identical logits.
+template <int NT, int CPB, int NB>
+FP4X_DEV void stage_int2(const WarpCtx& c, float (&acc)[NT][4]) {
+  constexpr int NACC = 4;
 #pragma unroll
-    for (int r = 0; r < RG; ++r) {
-      a[r][0] = lds128(c.a0 + (16 * r + c.g) * c.P0 + 64 * blk + 16 * c.tq);
-      a[r][1] = lds128(c.a0 + (16 * r + c.g + 8) * c.P0 + 64 * blk + 16 * c.tq);
-    }
+  for (int b = 0; b < NB; ++b) {
 #pragma unroll
-    for (int gi = 0; gi < 4; ++gi) {
-      // 16-k group index (within the chunk) of this thread's group gi, and its scale slot
-      const int g16 = 16 * blk + 4 * c.tq + gi;
-      const int sidx = g16 >> gshift;
-      uint32_t tlo[RG][2], thi[RG][2], W[RG][2];
+    for (int u = 0; u < CPB / 2; ++u) {
+      float accs[NACC][NT][4];
+      zero_accs<NT, NACC>(accs);
+      uint32_t rr[4];
+      ld_pair(c, b, 2 * u, rr[0], rr[1], rr[2], rr[3]);
+      const int C0 = b * CPB + 2 * u;
+      uint32_t s16[2][2];
 #pragma unroll
-      for (int r = 0; r < RG; ++r) {
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          const int row = 16 * r + c.g + 8 * q;
-          int2_table(lds16(c.sc + row * c.PS + 2 * sidx), tlo[r][q], thi[r][q]);
-          W[r][q] = gi == 0 ? a[r][q].x : gi == 1 ? a[r][q].y : gi == 2 ? a[r][q].z : a[r][q].w;
-        }
+      for (int cc = 0; cc < 2; ++cc) {
+        const int sidx = (4 * (C0 + cc) + c.tq) >> c.gshift;
+        s16[cc][0] = lds16(c.sc + (c.rbase + c.g) * c.SB + 2 * sidx);
+        s16[cc][1] = lds16(c.sc + (c.rbase + c.g + 8) * c.SB + 2 * sidx);
       }
+      uint32_t b0[8][NT], b1[8][NT];
 #pragma unroll
-      for (int p = 0; p < 4; ++p) {
-        uint32_t b0[NT], b1[NT];
-        load_b<NT>(c, 16 * blk + 4 * gi + p, b0, b1);
+      for (int s = 0; s < 8; ++s) load_b<NT>(c, 4 * C0 + s, b0[s], b1[s]);
 #pragma unroll
-        for (int r = 0; r < RG; ++r) {
+      for (int cc = 0; cc < 2; ++cc) {
+        uint32_t tlo[2], thi[2];
+        int2_table(s16[cc][0], tlo[0], thi[0]);
+        int2_table(s16[cc][1], tlo[1], thi[1]);
+        const uint32_t W[2] = {rr[2 * cc], rr[2 * cc + 1]};
+#pragma unroll
+        for (int p = 0; p < 4; ++p) {
           uint32_t A[4];
 #pragma unroll
           for (int q = 0; q < 2; ++q) {
-            const uint32_t z = (W[r][q] >> (2 * p)) & 0x03030303u;
+            const uint32_t z = (W[q] >> (2 * p)) & 0x03030303u;
             const uint32_t sl = z * 0x11u + 0x4040u;
             const uint32_t sh = __umulhi(z, 0x110000u) + 0x4040u;
-            A[q] = prmt(tlo[r][q], thi[r][q], sl);
-            A[2 + q] = prmt(tlo[r][q], thi[r][q], sh);
+            A[q] = prmt(tlo[q], thi[q], sl);
+            A[2 + q] = prmt(tlo[q], thi[q], sh);
           }
-#pragma unroll
-          for (int t = 0; t < NT; ++t) mma_bf16(acc[r][t], A, b0[t], b1[t], acc[r][t]);
+          mma_bf16_acc<NT>(accs[p], A, b0[4 * cc + p], b1[4 * cc + p]);
         }
       }
+      fold_accs<NT, NACC>(acc, accs);
     }
   }
 }
 
-template <int FMT, int NT, int RG>
-FP4X_DEV void compute_chunk(const ChunkCtx& c, float (&acc)[RG][NT][4]) {
-  if (FMT == FMT_MX8) chunk_mx8<NT, RG>(c, acc);
-  else if (FMT == FMT_W8) chunk_w8<NT, RG>(c, acc);
-  else if (FMT == FMT_W6) chunk_w6<NT, RG>(c, acc);
-  else if (FMT == FMT_NV4) chunk_nv4<NT, RG>(c, acc);
-  else if (FMT == FMT_BF16) chunk_bf16<NT, RG>(c, acc);
-  else chunk_int2<NT, RG>(c, acc);
+template <int FMT, int NT, int CPB, int NB>
+FP4X_DEV void stage_shape(const WarpCtx& c, float (&acc)[NT][4]) {
+  if (FMT == FMT_MX8) stage_mx8<NT, CPB, NB>(c, acc);
+  else if (FMT == FMT_W8) stage_w8<NT, CPB, NB>(c, acc);
+  else if (FMT == FMT_W6) stage_w6<NT, CPB, NB>(c, acc);
+  else if (FMT == FMT_NV4) stage_nv4<NT, CPB, NB>(c, acc);
+  else if (FMT == FMT_BF16) stage_bf16<NT, CPB, NB>(c, acc);
+  else stage_int2<NT, CPB, NB>(c, acc);
+}
+
+// stage shapes used by the planner: (128-byte boxes, 2 per stage), (128, 1), (64, 1)
+template <int FMT, int NT>
+FP4X_DEV void compute_stage(const WarpCtx& c, float (&acc)[NT][4]) {
+  if (c.BI0 == 128) {
+    if (c.NB0 == 2) stage_shape<FMT, NT, 8, 2>(c, acc);
+    else stage_shape<FMT, NT, 8, 1>(c, acc);
+  } else {
+    stage_shape<FMT, NT, 4, 1>(c, acc);
+  }
 }
 
 // ------------------------------------------------------------------------------------------------------
-// epilogues
+// epilogues (values v are this warp's 16 rows: c0,c1 row g; c2,c3 row g+8; columns 8t + 2tq + (0,1))
 // ------------------------------------------------------------------------------------------------------
 // hyper-connection down epilogue (fused and unfused paths share it): di = bf16(v); bot = bf16(t*sigmoid(t)),
 // t = bf16(f32(di) / hc), for columns < lr
@@ -570,247 +679,268 @@ FP4X_DEV float hc_gate_mean(const float* nrm_vals, const float* gates, int hc) {
   return bf16_round(p[0] / (float)hc);
 }
 
-template <int EPI, int NT, int RG>
-FP4X_DEV void run_epilogue(const GemvArgs& A, const GemvItem& it, int rt, const float (&v)[RG][NT][4], int g, int tq,
-                           float* scr) {
-  constexpr int RU = 16 * RG;
+template <int EPI, int NT>
+FP4X_DEV void run_epilogue(const GemvArgs& A, const GemvItem& it, int row0, const float (&v)[NT][4], int warp, int g,
+                           int tq, float* scr_all) {
+  constexpr int MP = 8 * NT;
   if (EPI == EPI_STORE || EPI == EPI_HEAD || EPI == EPI_HC_DOWN) {
 #pragma unroll
-    for (int r = 0; r < RG; ++r)
+    for (int t = 0; t < NT; ++t)
 #pragma unroll
-      for (int t = 0; t < NT; ++t)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int n = rt * RU + 16 * r + g + 8 * (e >> 1);
-          const int m = 8 * t + 2 * tq + (e & 1);
-          if (n < A.N && m < A.M) {
-            if (EPI == EPI_HC_DOWN) {
-              hc_down_store(reinterpret_cast<__nv_bfloat16*>(it.out), reinterpret_cast<__nv_bfloat16*>(it.out2),
-                            A.N, A.lr, A.hc, m, n, v[r][t][e]);
-            } else {
-              const float val = v[r][t][e] * A.post;
-              store_out(it.out, A.out_dtype, (int64_t)m * A.out_stride + n, val);
-              if (EPI == EPI_HEAD && it.out2)
-                reinterpret_cast<__nv_bfloat16*>(it.out2)[(int64_t)m * A.out_stride + n] = __float2bfloat16_rn(val);
-            }
+      for (int e = 0; e < 4; ++e) {
+        const int n = row0 + g + 8 * (e >> 1);
+        const int m = 8 * t + 2 * tq + (e & 1);
+        if (n < A.N && m < A.M) {
+          if (EPI == EPI_HC_DOWN) {
+            hc_down_store(reinterpret_cast<__nv_bfloat16*>(it.out), reinterpret_cast<__nv_bfloat16*>(it.out2), A.N,
+                          A.lr, A.hc, m, n, v[t][e]);
+          } else {
+            const float val = v[t][e] * A.post;
+            store_out(it.out, A.out_dtype, (int64_t)m * A.out_stride + n, val);
+            if (EPI == EPI_HEAD && it.out2)
+              reinterpret_cast<__nv_bfloat16*>(it.out2)[(int64_t)m * A.out_stride + n] = __float2bfloat16_rn(val);
           }
         }
-  } else {  // EPI_HC_UP: rows of this unit are hc streams x bj columns (interleaved); RU == hc * bj
-    constexpr int MPx = 8 * NT;
-    const int lane = g * 4 + tq;
-#pragma unroll
-    for (int r = 0; r < RG; ++r)
-#pragma unroll
-      for (int t = 0; t < NT; ++t)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int row = 16 * r + g + 8 * (e >> 1);
-          const int m = 8 * t + 2 * tq + (e & 1);
-          const float gl = bf16_round(v[r][t][e]);
-          scr[row * MPx + m] = bf16_round(sigmoidf_(gl));
-        }
-    __syncwarp();
-    const int bj = A.bj, hc = A.hc;
-    const int H = A.N / hc;
-    const __nv_bfloat16* nrm = reinterpret_cast<const __nv_bfloat16*>(A.nrm);
-    for (int o = lane; o < bj * A.M; o += 32) {
-      const int m = o / bj, c = o - m * bj;
-      const int col = rt * bj + c;
-      float nv[8], gv[8];
-      for (int s = 0; s < hc; ++s) {
-        nv[s] = __bfloat162float(nrm[(int64_t)m * A.nrm_stride + s * H + col]);
-        gv[s] = scr[(s * bj + c) * MPx + m];
       }
-      reinterpret_cast<__nv_bfloat16*>(it.out)[(int64_t)m * A.out_stride + col] =
-          __float2bfloat16_rn(hc_gate_mean(nv, gv, hc));
+  } else {  // EPI_HC_UP: interleaved blocks of hc * bj rows (16 rows: one warp; 32 rows: a warp pair)
+    float* scr = scr_all + warp * 16 * MP;
+#pragma unroll
+    for (int t = 0; t < NT; ++t)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int r = g + 8 * (e >> 1);
+        const int m = 8 * t + 2 * tq + (e & 1);
+        scr[r * MP + m] = bf16_round(sigmoidf_(bf16_round(v[t][e])));
+      }
+    const int rows = A.hc * A.bj;
+    const int lane = 4 * g + tq;
+    int first_warp = warp, nwarps = 1;
+    if (rows == 32) {
+      first_warp = warp & ~1;
+      nwarps = 2;
+      named_bar(2 + (warp >> 1), 64);
+    } else {
+      __syncwarp();
     }
-    __syncwarp();
+    const float* bscr = scr_all + first_warp * 16 * MP;  // the block's rows, contiguous over the warp pair
+    const int blk_row0 = row0 - 16 * (warp - first_warp);
+    if (blk_row0 < A.N) {
+      const int jb = blk_row0 / rows;  // interleave block index
+      const int H = A.N / A.hc;
+      const __nv_bfloat16* nrm = reinterpret_cast<const __nv_bfloat16*>(A.nrm);
+      const int nout = A.bj * A.M;
+      for (int o = lane + 32 * (warp - first_warp); o < nout; o += 32 * nwarps) {
+        const int m = o / A.bj, cidx = o - m * A.bj;
+        const int col = jb * A.bj + cidx;
+        float nv[8], gv[8];
+        for (int s = 0; s < A.hc; ++s) {
+          nv[s] = __bfloat162float(nrm[(int64_t)m * A.nrm_stride + s * H + col]);
+          gv[s] = bscr[(s * A.bj + cidx) * MP + m];
+        }
+        reinterpret_cast<__nv_bfloat16*>(it.out)[(int64_t)m * A.out_stride + col] =
+            __float2bfloat16_rn(hc_gate_mean(nv, gv, A.hc));
+      }
+    }
+    if (rows == 32) named_bar(2 + (warp >> 1), 64);
+    else __syncwarp();
   }
 }
 
 // ------------------------------------------------------------------------------------------------------
 // the kernel
 // ------------------------------------------------------------------------------------------------------
-template <int FMT>
-FP4X_DEV void issue_chunk(const GemvArgs& A, const GemvItem& it, int64_t u, int k_panel0, uint32_t stage,
-                          uint32_t bar, int lane, int RU) {
-  constexpr FmtGeom G = fmt_geom(FMT);
-  const int rt = (int)(u / A.NCH), c = (int)(u - (int64_t)rt * A.NCH);
-  const int k0 = k_panel0 + c * A.KC;
-  const int pb0 = A.KC * G.n0 / G.d0;
-  const int pb1 = G.n1 ? A.KC * G.n1 / G.d1 : 0;
-  const int sd = FMT == FMT_INT2 ? A.group / 2 : G.sd;
-  const int sbytes = G.sn ? A.KC * G.sn / sd : 0;
-  if (lane == 0) mbar_arrive_expect_tx(bar, (uint32_t)(RU * (pb0 + pb1)));
-  __syncwarp();
-  const int row0 = rt * RU;
-  for (int r = lane; r < RU; r += 32) {
-    const int row = min(row0 + r, A.N - 1);
-    bulk_g2s(stage + r * A.P0, it.p0 + (int64_t)row * A.ld0 + (int64_t)k0 * G.n0 / G.d0, pb0, bar);
-    if constexpr (G.n1 != 0) bulk_g2s(stage + RU * A.P0 + r * A.P1, it.p1 + (int64_t)row * A.ld1 + (int64_t)k0 * G.n1 / G.d1, pb1, bar);
-  }
-  if constexpr (G.sn != 0) {
-    const int wpr = sbytes / 4;
-    const uint32_t sbase = stage + RU * (A.P0 + A.P1);
-    const int64_t koff = (int64_t)k0 * G.sn / sd;
-    for (int w = lane; w < RU * wpr; w += 32) {
-      const int r = w / wpr, cw = w - r * wpr;
-      const int row = min(row0 + r, A.N - 1);
-      cp_async4(sbase + r * A.PS + 4 * cw, it.sc + (int64_t)row * A.lds + koff + 4 * cw);
-    }
-  }
-  cp_async_arrive_noinc(bar);
-}
-
-template <int FMT, int NT, int RG, int EPI>
-__global__ void __launch_bounds__(kThreads, 1) gemv_kernel(const __grid_constant__ GemvArgs A) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  constexpr int RU = 16 * RG;
+template <int FMT, int NT, int EPI>
+__global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ GemvArgs A) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  // stages need 1024-byte alignment for the swizzled TMA tiles; the host adds 1 KB of slack
+  uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   constexpr int MP = 8 * NT;
   constexpr FmtGeom G = fmt_geom(FMT);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, g = lane >> 2, tq = lane & 3;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int p = blockIdx.y, b = blockIdx.z;
-  GemvItem it = A.item;
-  if (A.items4) {
-    const void* const* e = A.items4 + 4 * b;
-    it.x = e[0];
-    it.p0 = (const uint8_t*)e[1];
-    it.sc = (const uint8_t*)e[2];
-    it.out = (void*)e[3];
-  }
   const int k_panel0 = p * A.KPW;
+  GemvItem it = A.item;
+  const CUtensorMap* tm0 = &A.tm0;
+  if (A.batch) {
+    const BatchEntry* e = A.batch + b;
+    tm0 = &e->tm0;
+    it.x = e->x;
+    it.sc = e->sc;
+    it.out = e->out;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + A.smem_misc + 128);
+  const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kMaxStages);
+  const uint32_t xbar = smem_u32(bars + 2 * kMaxStages);
+  const int CPP = A.CPP;
+  const int cta = blockIdx.x;
+  const int64_t Up = A.whole ? (int64_t)A.RT : (int64_t)A.RT * A.NCH;
+  const int64_t u_begin = A.whole ? range_begin(A.RT, CPP, cta) * A.NCH : range_begin(Up, CPP, cta);
+  const int64_t u_end = A.whole ? range_begin(A.RT, CPP, cta + 1) * A.NCH : range_begin(Up, CPP, cta + 1);
+  const int64_t nunits = u_end - u_begin;
 
-  const uint32_t bars = smem_u32(smem) + warp * kMaxStages * 8;
-  const uint32_t stages = smem_u32(smem + A.smem_stage) + warp * A.NS * A.STG;
-  const int Wp = A.CPP * kWarps;
-  const int wg = blockIdx.x * kWarps + warp;
-  const int64_t Up = (int64_t)A.RT * A.NCH;
-  const int64_t u_begin = A.whole ? range_begin(A.RT, Wp, wg) * A.NCH : range_begin(Up, Wp, wg);
-  const int64_t u_end = A.whole ? range_begin(A.RT, Wp, wg + 1) * A.NCH : range_begin(Up, Wp, wg + 1);
-
-  if (lane == 0) {
-    for (int s = 0; s < A.NS; ++s) mbar_init(bars + 8 * s, 33);
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < A.NS; ++s) {
+      mbar_init(full0 + 8 * s, 33);
+      mbar_init(empty0 + 8 * s, kCWarps);
+    }
+    mbar_init(xbar, 1);
     mbar_init_fence();
   }
-  __syncwarp();
-  for (int64_t q = 0; q < A.NS && u_begin + q < u_end; ++q)
-    issue_chunk<FMT>(A, it, u_begin + q, k_panel0, stages + (uint32_t)q * A.STG, bars + 8 * (uint32_t)q, lane, RU);
-
-  pdl_wait();
-  stage_activations<FMT>(A, it, smem, MP, k_panel0);
   __syncthreads();
+
+  if (warp == kCWarps) {
+    // ---------------- producer warp ----------------
+    pdl_launch_dependents();
+    const int tx = kRB * (A.NB0 * A.BI0 + (G.n1 ? A.BI1 : 0));
+    const int scw = A.scw;
+    const int words_per_row = G.sn ? A.SB / scw : 0;
+    const int sd = FMT == FMT_INT2 ? A.group / 2 : G.sd;
+    for (int64_t q = 0; q < nunits; ++q) {
+      const int s = (int)(q % A.NS);
+      if (q >= A.NS) {
+        if (!mbar_wait_bounded(empty0 + 8 * s, (uint32_t)(((q / A.NS) - 1) & 1), A.err)) break;
+      }
+      const int64_t u = u_begin + q;
+      const int blk = (int)(u / A.NCH), chunk = (int)(u - (int64_t)blk * A.NCH);
+      const int k0 = k_panel0 + chunk * A.KC;
+      const uint32_t stage = smem_u32(base) + (uint32_t)s * A.STG;
+      const uint32_t bar = full0 + 8 * s;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(bar, (uint32_t)tx);
+        const int xb0 = k0 * G.n0 / G.d0;
+        for (int bx = 0; bx < A.NB0; ++bx)
+          tma_load_2d(stage + bx * kRB * A.BI0, tm0, xb0 + bx * A.BI0, blk * kRB, bar);
+        if constexpr (G.n1 != 0) tma_load_2d(stage + A.off_p1, &A.tm1, k0 * G.n1 / G.d1, blk * kRB, bar);
+      }
+      if constexpr (G.sn != 0) {
+        const int64_t koff = (int64_t)k0 * G.sn / sd;
+        const uint32_t sbase = stage + A.off_sc;
+        for (int w = lane; w < kRB * words_per_row; w += 32) {
+          const int r = w / words_per_row, cw = w - r * words_per_row;
+          const int row = min(blk * kRB + r, A.N - 1);
+          const uint8_t* src = it.sc + (int64_t)row * A.lds + koff + (int64_t)cw * scw;
+          const uint32_t dst = sbase + r * A.SB + cw * scw;
+          if (scw == 16) cp_async16(dst, src);
+          else if (scw == 8) cp_async8(dst, src);
+          else cp_async4(dst, src);
+        }
+      }
+      cp_async_arrive_noinc(bar);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+    return;
+  }
+
+  // ---------------- consumer warps ----------------
+  const int g = lane >> 2, tq = lane & 3;
+  pdl_wait();
+  stage_activations<FMT>(A, it, base, MP, k_panel0, xbar);
+  named_bar(1, kCWarps * 32);
   pdl_launch_dependents();
 
-  const float* xsc = reinterpret_cast<const float*>(smem + kWarps * kMaxStages * 8);
-  float* scr = reinterpret_cast<float*>(smem + A.smem_scr) + warp * RU * MP;
-  ChunkCtx cc;
-  cc.P0 = A.P0; cc.P1 = A.P1; cc.PS = A.PS; cc.KC = A.KC; cc.XP = A.XP; cc.g = g; cc.tq = tq; cc.group = A.group;
-  const uint32_t xrow = smem_u32(smem + A.smem_x) + g * A.XP + tq * 8;
+  const float* xsc = reinterpret_cast<const float*>(base + A.smem_misc);
+  float* scr = reinterpret_cast<float*>(base + A.smem_scr);
+  WarpCtx wc;
+  wc.BI0 = A.BI0; wc.BI1 = A.BI1; wc.NB0 = A.NB0; wc.SB = A.SB; wc.XP = A.XP;
+  wc.g = g; wc.tq = tq; wc.rbase = 16 * warp;
+  wc.gshift = A.group == 32 ? 1 : 0;
+  {
+    const int r = 16 * warp + (lane & 7) + 8 * ((lane >> 3) & 1);
+    wc.lrow0 = (uint32_t)(r * A.BI0);
+    wc.lswz = A.BI0 == 128 ? (r & 7) : ((r >> 1) & 3);
+    wc.lsel = lane >> 4;
+  }
+  const uint32_t xrow = smem_u32(base + A.smem_x) + g * A.XP + tq * 8;
+  const int steps_per_stage = A.KC / 16;
 
-  float acc[RG][NT][4];
-  zero_acc<NT, RG>(acc);
-  int cur_rt = -1;
+  float acc[NT][4];
+  zero4<NT>(acc);
+  int cur = -1;
   bool ok = true;
 
-  auto flush = [&](int rt) {
-    // remove the activation scale (exact power of two) per token column
+  auto flush = [&](int blk) {
     if (G.xf16) {
 #pragma unroll
-      for (int r = 0; r < RG; ++r)
+      for (int t = 0; t < NT; ++t)
 #pragma unroll
-        for (int t = 0; t < NT; ++t)
-#pragma unroll
-          for (int e = 0; e < 4; ++e) acc[r][t][e] *= xsc[MP + 8 * t + 2 * tq + (e & 1)];
+        for (int e = 0; e < 4; ++e) acc[t][e] *= xsc[MP + 8 * t + 2 * tq + (e & 1)];
     }
-    const int64_t uf = (int64_t)rt * A.NCH, ul = uf + A.NCH - 1;
-    const int wf = A.whole ? wg : owner_of(uf, Up, Wp), wl = A.whole ? wg : owner_of(ul, Up, Wp);
-    const int segs = wl - wf + 1;
+    const int row0 = blk * kRB + 16 * warp;
+    int cf, cl;
+    if (A.whole) {
+      cf = cl = cta;
+    } else {
+      const int64_t uf = (int64_t)blk * A.NCH, ul = uf + A.NCH - 1;
+      cf = owner_of(uf, Up, CPP);
+      cl = owner_of(ul, Up, CPP);
+    }
+    const int segs = cl - cf + 1;
     if (A.KP == 1 && segs == 1) {
-      run_epilogue<EPI, NT, RG>(A, it, rt, acc, g, tq, scr);
+      run_epilogue<EPI, NT>(A, it, row0, acc, warp, g, tq, scr);
       return;
     }
-    auto slot_of = [&](int pp, int w) -> int64_t {
-      if (A.KP == 1) {  // at most two shared tiles per warp: its first (slot 0) and last (slot 1)
-        const int first_rt = (int)(range_begin(Up, Wp, w) / A.NCH);
-        return ((int64_t)b * Wp + w) * 2 + (rt == first_rt ? 0 : 1);
+    auto slot_of = [&](int pp, int cc) -> int64_t {
+      int64_t s;
+      if (A.KP == 1) {  // a CTA shares at most two blocks: its first (slot 0) and its last (slot 1)
+        const int first_blk = (int)(range_begin(Up, CPP, cc) / A.NCH);
+        s = ((int64_t)b * CPP + cc) * 2 + (blk == first_blk ? 0 : 1);
+      } else {
+        s = (((int64_t)b * A.KP + pp) * A.RT + blk) * A.SMAX + (cc - cf);
       }
-      return (((int64_t)b * A.KP + pp) * A.RT + rt) * A.SMAX + (w - wf);
+      return s * kCWarps + warp;
     };
-    float* mine = A.ws + slot_of(p, wg) * (RU * MP);
+    float* mine = A.ws + slot_of(p, cta) * (16 * MP);
 #pragma unroll
-    for (int r = 0; r < RG; ++r)
-#pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        const int row = 16 * r + g, m = 8 * t + 2 * tq;
-        __stcg(reinterpret_cast<float2*>(mine + row * MP + m), make_float2(acc[r][t][0], acc[r][t][1]));
-        __stcg(reinterpret_cast<float2*>(mine + (row + 8) * MP + m), make_float2(acc[r][t][2], acc[r][t][3]));
-      }
+    for (int t = 0; t < NT; ++t) {
+      const int m = 8 * t + 2 * tq;
+      __stcg(reinterpret_cast<float2*>(mine + g * MP + m), make_float2(acc[t][0], acc[t][1]));
+      __stcg(reinterpret_cast<float2*>(mine + (g + 8) * MP + m), make_float2(acc[t][2], acc[t][3]));
+    }
     __threadfence();
     __syncwarp();
+    int* semp = A.sem + ((int64_t)b * A.RT + blk) * kCWarps + warp;
     int last = 0;
-    if (lane == 0) {
-      const int old = atomicAdd(A.sem + (int64_t)b * A.RT + rt, 1);
-      last = (old == A.KP * segs - 1);
-    }
+    if (lane == 0) last = (atomicAdd(semp, 1) == A.KP * segs - 1);
     last = __shfl_sync(0xffffffffu, last, 0);
     if (!last) return;
     __threadfence();
-    float tot[RG][NT][4];
-    zero_acc<NT, RG>(tot);
+    float tot[NT][4];
+    zero4<NT>(tot);
     for (int pp = 0; pp < A.KP; ++pp)
-      for (int w = wf; w <= wl; ++w) {
-        const float* src = A.ws + slot_of(pp, w) * (RU * MP);
+      for (int cc = cf; cc <= cl; ++cc) {
+        const float* src = A.ws + slot_of(pp, cc) * (16 * MP);
 #pragma unroll
-        for (int r = 0; r < RG; ++r)
-#pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            const int row = 16 * r + g, m = 8 * t + 2 * tq;
-            const float2 lo = __ldcg(reinterpret_cast<const float2*>(src + row * MP + m));
-            const float2 hi = __ldcg(reinterpret_cast<const float2*>(src + (row + 8) * MP + m));
-            tot[r][t][0] += lo.x; tot[r][t][1] += lo.y; tot[r][t][2] += hi.x; tot[r][t][3] += hi.y;
-          }
+        for (int t = 0; t < NT; ++t) {
+          const int m = 8 * t + 2 * tq;
+          const float2 lo = __ldcg(reinterpret_cast<const float2*>(src + g * MP + m));
+          const float2 hi = __ldcg(reinterpret_cast<const float2*>(src + (g + 8) * MP + m));
+          tot[t][0] += lo.x; tot[t][1] += lo.y; tot[t][2] += hi.x; tot[t][3] += hi.y;
+        }
       }
-    run_epilogue<EPI, NT, RG>(A, it, rt, tot, g, tq, scr);
-    if (lane == 0) atomicExch(A.sem + (int64_t)b * A.RT + rt, 0);
+    run_epilogue<EPI, NT>(A, it, row0, tot, warp, g, tq, scr);
+    if (lane == 0) atomicExch(semp, 0);
   };
 
-  for (int64_t u = u_begin; u < u_end; ++u) {
-    const int64_t q = u - u_begin;
-    const int st = (int)(q % A.NS);
-    const uint32_t parity = (uint32_t)((q / A.NS) & 1);
-    const int rt = (int)(u / A.NCH), c = (int)(u - (int64_t)rt * A.NCH);
-    if (rt != cur_rt) {
-      if (cur_rt >= 0) flush(cur_rt);
-      zero_acc<NT, RG>(acc);
-      cur_rt = rt;
+  for (int64_t q = 0; q < nunits; ++q) {
+    const int s = (int)(q % A.NS);
+    const int64_t u = u_begin + q;
+    const int blk = (int)(u / A.NCH), chunk = (int)(u - (int64_t)blk * A.NCH);
+    if (blk != cur) {
+      if (cur >= 0) flush(cur);
+      zero4<NT>(acc);
+      cur = blk;
     }
-    if (!mbar_wait_bounded(bars + 8 * st, parity, A.err)) { ok = false; break; }
-    const uint32_t sbase = stages + (uint32_t)st * A.STG;
-    cc.a0 = sbase;
-    cc.a1 = sbase + RU * A.P0;
-    cc.sc = sbase + RU * (A.P0 + A.P1);
-    cc.xb = xrow + c * (A.KC / 16) * 32;
-    compute_chunk<FMT, NT, RG>(cc, acc);
-    fence_proxy_async_smem();
+    if (!mbar_wait_bounded(full0 + 8 * s, (uint32_t)((q / A.NS) & 1), A.err)) { ok = false; break; }
+    const uint32_t stage = smem_u32(base) + (uint32_t)s * A.STG;
+    wc.p0 = stage;
+    wc.p1 = stage + A.off_p1;
+    wc.sc = stage + A.off_sc;
+    wc.xb = xrow + chunk * steps_per_stage * 32;
+    compute_stage<FMT, NT>(wc, acc);
     __syncwarp();
-    if (u + A.NS < u_end) issue_chunk<FMT>(A, it, u + A.NS, k_panel0, sbase, bars + 8 * st, lane, RU);
+    if (lane == 0) mbar_arrive(empty0 + 8 * s);
   }
-  if (ok && cur_rt >= 0) flush(cur_rt);
-  if (!ok) {
-    // a stage never completed (error already recorded): wait, bounded, for the copies this warp still has in
-    // flight so that nothing lands in shared memory after the CTA has gone, then leave
-    asm volatile("cp.async.wait_all;" ::: "memory");
-    for (int s = 0; s < A.NS; ++s) {
-      uint32_t par = 0;
-      while (par < 2 && !mbar_try_wait(bars + 8 * s, par)) ++par;
-    }
-    const uint64_t t0 = global_ns();
-    while (global_ns() - t0 < 100000000ull) {
-      bool all = true;
-      for (int s = 0; s < A.NS; ++s) all = all && (mbar_try_wait(bars + 8 * s, 0) || mbar_try_wait(bars + 8 * s, 1));
-      if (all) break;
-    }
-  }
+  if (ok && cur >= 0) flush(cur);
 }
 
 }  // namespace fp4x

@@ -5,7 +5,7 @@
 
 #include <string>
 
-#include "../../include/fp4x.h"
+#include "fp4x.h"
 
 namespace fp4x {
 
@@ -16,6 +16,7 @@ int fail(int code, const std::string& msg);
 struct DeviceFacts {
   int sms;
   int smem_optin;  // max dynamic shared memory per block (opt-in)
+  int smem_sm;     // shared memory per multiprocessor
 };
 const DeviceFacts& device_facts();
 

@@ -159,8 +159,8 @@ def int2_logits(x, P, S, N_rows=None, BN=64, BK=512, nw=4, RS=None, out_dtype=to
 class W8Batch:
     """Batched W8 GEMVs of one shape in one launch (the router gates, P:258-272 with FP4X_GATE=w8).
 
-    The device pointer table is built once from the given activation/output buffers and weights, so the launch
-    can be captured in a CUDA graph; callers write new activations into the same `xs` buffers."""
+    The device table (TMA descriptors of the weights plus the activation/output pointers) is built once from the
+    given buffers, so the launch itself needs no host work; callers write new activations into the same `xs`."""
 
     def __init__(self, xs, qs, ss, outs=None, out_dtype=torch.bfloat16):
         assert len(xs) == len(qs) == len(ss) and len(qs) > 0
@@ -175,13 +175,18 @@ class W8Batch:
         self.out_dtype = out_dtype
         self.outs = outs if outs is not None else [torch.empty((self.m, self.n), dtype=out_dtype, device=dev)
                                                    for _ in qs]
-        tab = [[x.data_ptr(), q.data_ptr(), s.data_ptr(), o.data_ptr()]
-               for x, q, s, o in zip(self.xs, self.qs, self.ss, self.outs)]
-        self.table = torch.tensor(tab, dtype=torch.int64, device=dev)
+        items = (N.W8Item * len(qs))()
+        for i, (x, q, s, o) in enumerate(zip(self.xs, self.qs, self.ss, self.outs)):
+            items[i] = N.W8Item(x.data_ptr(), q.data_ptr(), s.data_ptr(), o.data_ptr())
+        nbytes = N.lib().fp4x_w8_batch_table_bytes(len(qs))
+        self.table = torch.empty(nbytes + 64, dtype=torch.uint8, device=dev)
+        off = (-self.table.data_ptr()) % 64
+        self.table_view = self.table[off:off + nbytes]
+        N.call("fp4x_w8_batch_prepare", items, len(qs), self.n, self.k, N.ptr(self.table_view), nbytes)
         self.ws, self.cnt = N.scratch(N.FMT_W8, self.m, self.n, self.k, dev, len(qs))
 
     def run(self):
-        N.call("fp4x_w8_linear_batched", N.ptr(self.table), len(self.qs), self.xs[0].stride(0),
+        N.call("fp4x_w8_linear_batched", N.ptr(self.table_view), len(self.qs), self.xs[0].stride(0),
                self.outs[0].stride(0), N.dtype_code(self.out_dtype), self.m, self.n, self.k,
                *N.scratch_args(self.ws, self.cnt), N.stream_of(self.table))
         return self.outs

@@ -29,12 +29,18 @@ _sz = ctypes.c_size_t
 _f32 = ctypes.c_float
 _ip = ctypes.POINTER(ctypes.c_int32)
 
+
+class W8Item(ctypes.Structure):
+    """fp4x_w8_item of include/fp4x.h."""
+    _fields_ = [("x", ctypes.c_void_p), ("q", ctypes.c_void_p), ("s", ctypes.c_void_p), ("out", ctypes.c_void_p)]
+
 # argument signatures of every exported entry point (must match include/fp4x.h)
 _SIGS = {
     "fp4x_version": ([], _i32),
     "fp4x_last_error_message": ([], ctypes.c_char_p),
     "fp4x_device_error": ([_p, _i32, ctypes.POINTER(ctypes.c_int)], _i32),
     "fp4x_gemv_query": ([_i32, _i64, _i64, _i64, _i64, _i32, ctypes.POINTER(_sz), ctypes.POINTER(_i64)], _i32),
+    "fp4x_plan_describe": ([_i32, _i64, _i64, _i64, _i64, _i32, _i32, ctypes.c_char_p, _sz], _i32),
     "fp4x_mx8_linear": ([_p, _i64, _p, _p, _p, _i64, _i32, _i64, _i64, _i64, _p, _sz, _p, _i64, _p], _i32),
     "fp4x_bf16_linear": ([_p, _i64, _p, _p, _i64, _i32, _i64, _i64, _i64, _p, _sz, _p, _i64, _p], _i32),
     "fp4x_nv4_linear": ([_p, _i64, _p, _p, _f32, _p, _i64, _i32, _i64, _i64, _i64, _p, _sz, _p, _i64, _p], _i32),
@@ -42,6 +48,8 @@ _SIGS = {
     "fp4x_w6_linear": ([_p, _i64, _p, _p, _p, _p, _i64, _i32, _i64, _i64, _i64, _p, _sz, _p, _i64, _p], _i32),
     "fp4x_int2_logits": ([_p, _i64, _p, _p, _i32, _p, _i64, _i32, _p, _i64, _i64, _i64, _p, _sz, _p, _i64, _p],
                          _i32),
+    "fp4x_w8_batch_table_bytes": ([_i64], _sz),
+    "fp4x_w8_batch_prepare": ([_p, _i64, _i64, _i64, _p, _sz], _i32),
     "fp4x_w8_linear_batched": ([_p, _i64, _i64, _i64, _i32, _i64, _i64, _i64, _p, _sz, _p, _i64, _p], _i32),
     "fp4x_hc_down": ([_p, _i64, _p, _p, _p, _p, _i64, _i64, _i64, _i64, _i64, _p, _sz, _p, _i64, _p], _i32),
     "fp4x_hc_up": ([_p, _i64, _p, _p, _p, _i64, _p, _i64, _i64, _i64, _i64, _i64, _p], _i32),
@@ -167,6 +175,13 @@ def topk_scratch(m, v, c, device):
     nc = _i64(0)
     call("fp4x_topk_query", m, v, c, ctypes.byref(ws), ctypes.byref(nc))
     return (torch.empty(ws.value, dtype=torch.uint8, device=device), counters(device, nc.value))
+
+
+def plan(fmt, m, n, k, batch=1, group=16, whole=False):
+    """The launch plan the library picks for a GEMV of this shape (diagnostic text)."""
+    buf = ctypes.create_string_buffer(512)
+    call("fp4x_plan_describe", fmt, m, n, k, batch, group, 1 if whole else 0, buf, 512)
+    return buf.value.decode()
 
 
 def device_error(clear=True, device=None):
