@@ -1,0 +1,669 @@
+#!/usr/bin/env python3
+"""Benchmark of the fp4x decode-GEMV path on B200: one JSON line on rank 0.
+
+Workload (the synthetic M=3 decode step of the baseline's fifth configuration): 48 layers, each
+  NVFP4 qkvz GEMV 16384x2560 -> W6 g32 GEMV 2560x4096 (input: the first 4096 qkvz columns) -> W6 g32 GEMV
+  4096x2560, an int8 g64 router gate 512x2560, and the fused hyper-connection W8 mixer (down 512x10240 split-K
+  with the SiLU epilogue, up 10240x512 with the sigmoid-gate / stream-mean epilogue, whose output is the next
+  layer's hidden row),
+then the fast LM head over 248,320 rows (INT2 g16 coarse pass, exact top-512, exact MXFP8 rescore, argmax).
+Weights are random (N(0, 0.02) quantized with the product quantizers, seeded CUDA generator); activations
+N(0, 1).  The step is captured once in a CUDA graph and replayed.  Every step streams 2.79 GB of packed weights,
+more than 20x the 126 MB L2, so no flush is needed between steps.
+
+value      aggregate algorithmic HBM GB/s of the step over all ranks (packed weights + scales read once per step,
+           activations and outputs not counted) / the device time of a step (CUDA events, max over ranks).
+e2e        the same metric with, inside the timed region of every step, the host->device copy of the step's
+           inputs (hidden row and hyper-connection streams, pinned host memory) and the device->host copy of its
+           result (top-512 ids and argmax).
+roofline   the kernel class with the largest share of the step, timed alone (CUDA events, graph of its 48
+           launches) against the measured HBM copy bandwidth in MEASURED_PEAKS.json.
+cpu_baseline / --impl reference
+           the CPU oracle (numpy restatement of the reference's dequantize-then-matmul path) on a bounded sample
+           of the same step: one layer plus 1/64 of the head rows and the M x 512 rescore rows.
+
+Multi-GPU (torchrun): every rank runs its own replica of the 48 layers (they do not shard) and 1/N of the head
+rows; the per-shard top-512 candidates are exchanged with one NCCL all-gather and merged on every rank.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG = os.path.join(ROOT, "qwen3.8-flash-next-fp4-local-spark_b200")
+sys.path.insert(0, PKG)
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = "decode GEMV HBM GB/s (% of 8 TB/s) at M=1..16; ms per synthetic M=3 decode step"
+HID, QKVZ, W6_IN, GATE, HCN, LR, VOCAB, CAND = 2560, 16384, 4096, 512, 4, 512, 248320, 512
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ----------------------------------------------------------------------------------------------------------
+# algorithmic bytes (packed weights + scales, read once)
+# ----------------------------------------------------------------------------------------------------------
+def bytes_nv4(n, k):
+    return n * k // 2 + n * k // 16 + 4
+
+
+def bytes_w6(n, k):
+    return n * k // 2 + n * k // 4 + n * k // 16
+
+
+def bytes_w8(n, k):
+    return n * k + n * k // 16
+
+
+def bytes_int2(v, k, group=16):
+    return v * k // 4 + v * k * 2 // group
+
+
+def bytes_rescore(m, c, k):
+    return m * c * (k + k // 32)
+
+
+CLASSES = {  # kernel class -> algorithmic bytes of one launch
+    "nv4_qkvz": bytes_nv4(QKVZ, HID),
+    "w6_2560x4096": bytes_w6(HID, W6_IN),
+    "w6_4096x2560": bytes_w6(W6_IN, HID),
+    "w8_gate": bytes_w8(GATE, HID),
+    "hc_down": bytes_w8(LR, HCN * HID),
+    "hc_up": bytes_w8(HCN * HID, LR),
+}
+LAYER_BYTES = sum(CLASSES.values())
+
+
+def head_bytes(m, vocab_rows):
+    return bytes_int2(vocab_rows, HID) + bytes_rescore(m, CAND, HID)
+
+
+# ----------------------------------------------------------------------------------------------------------
+# distributed plumbing
+# ----------------------------------------------------------------------------------------------------------
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_dist(world, local, backend):
+    import datetime
+    import torch.distributed as dist
+    if world > 1 and not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group(backend, timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local) if backend == "nccl" else None)
+    return dist
+
+
+def max_over_ranks(v, world, device):
+    if world == 1:
+        return v
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(world, device=None):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier(device_ids=[device.index] if device is not None and device.type == "cuda" else None)
+
+
+# ----------------------------------------------------------------------------------------------------------
+# clocks (nvidia-smi sampled during the timed region)
+# ----------------------------------------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device):
+        self.samples = []
+        self.proc = None
+        self.window = None
+        cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50"]
+        visible = os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",")
+        index = device.index or 0
+        if visible[0] != "" and index < len(visible):
+            cmd += ["-i", visible[index].strip()]
+        else:
+            cmd += ["-i", str(index)]
+        try:
+            self.proc = subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except (OSError, ValueError):
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.samples.append((time.time(), line.strip()))
+
+    def mark(self, t0, t1):
+        self.window = (t0, t1)
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.12)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        rows = []
+        for ts, line in self.samples:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) != 8:
+                continue
+            try:
+                rows.append((ts, float(parts[0]), float(parts[1]), parts[3:]))
+            except ValueError:
+                continue
+        if not rows:
+            return None
+        t0, t1 = self.window or (rows[0][0], rows[-1][0])
+        inside = [r for r in rows if t0 - 0.06 <= r[0] <= t1 + 0.06] or [min(rows, key=lambda r: abs(r[0] - t1))]
+        names = ("active", "hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        reasons = set()
+        for r in inside:
+            for name, val in zip(names[1:], r[3][1:]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(r[1] for r in inside), "sm_max_mhz": max(r[2] for r in inside),
+                "reasons": sorted(reasons), "samples": len(inside)}
+
+
+# ----------------------------------------------------------------------------------------------------------
+# the synthetic decode step
+# ----------------------------------------------------------------------------------------------------------
+class DecodeStep:
+    """Random-init weights of the step, resident in HBM, and the step itself through the public API."""
+
+    def __init__(self, device, m, layers, rank, world, seed=0):
+        import fp4x_kernels as F
+        from fp4x_shard import ShardedFastHead, shard_range
+        self.F = F
+        self.dev = device
+        self.m = m
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+
+        def w(n, k):
+            return torch.randn(n, k, device=device, generator=g) * 0.02
+
+        self.layers = []
+        for _ in range(layers):
+            L = {}
+            L["nv4"] = F.quantize_nv4(w(QKVZ, HID))
+            L["w6a"] = F.quantize_w6(w(HID, W6_IN))
+            L["w6b"] = F.quantize_w6(w(W6_IN, HID))
+            L["gate"] = F.quantize_w8(w(GATE, HID))
+            L["qd"], L["sd"] = F.quantize_w8(w(LR, HCN * HID))
+            qu, su = F.quantize_w8(w(HCN * HID, LR))
+            L["qi"], L["si"] = F.HCFused.interleave_up(qu, su, HCN, 8)
+            del qu, su
+            self.layers.append(L)
+        # head rows of this rank
+        self.v0, self.v1 = shard_range(VOCAB, rank, world)
+        rows = self.v1 - self.v0
+        codes, sc, P, S = [], [], [], []
+        for a in range(0, rows, 32768):
+            b = min(rows, a + 32768)
+            c_, s_ = F.quantize_mx8(w(b - a, HID))
+            p_, q_ = F.quantize_int2(F.mx8_dequant(c_, s_), group=16)
+            codes.append(c_); sc.append(s_); P.append(p_); S.append(q_)
+        self.head = ShardedFastHead(torch.cat(P), torch.cat(S), torch.cat(codes), torch.cat(sc), VOCAB, rank, world,
+                                    C=CAND)
+        del codes, sc, P, S
+        self.world = world
+        self.fx = F.HCFused(device, n_down=LR)
+        gx = torch.Generator(device=device)
+        gx.manual_seed(seed + 1)
+        self.h0 = torch.randn(m, HID, device=device, generator=gx).to(torch.bfloat16)
+        self.streams = torch.randn(m, HCN * HID, device=device, generator=gx).to(torch.bfloat16)
+        self.graph = None
+        self.result = None
+        torch.cuda.synchronize(device)
+
+    # one layer through the drop-in API
+    def layer(self, L, h):
+        F = self.F
+        q = F.nv4_linear(h, *L["nv4"])
+        o = F.w6_linear(q[:, :W6_IN], *L["w6a"])
+        F.w6_linear(o, *L["w6b"])
+        F.w8_linear(h, *L["gate"])
+        _, bot = self.fx.down(self.streams, L["qd"], L["sd"], LR, HCN)
+        return self.F.HCFused.up(bot, L["qi"], L["si"], self.streams, HCN, (8, 64, 8))
+
+    def body(self):
+        h = self.h0
+        for L in self.layers:
+            h = self.layer(L, h)
+        coarse, exact, gidx, _ = self.head.local(h)
+        return coarse, exact, gidx
+
+    def capture(self):
+        """Capture the layers and the local head in one graph; returns the number of library kernels per step."""
+        import fp4x_native as N
+        self.body()  # eager run: sizes the persistent counters, loads modules
+        torch.cuda.synchronize(self.dev)
+        s = torch.cuda.Stream(self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        self.graph = torch.cuda.CUDAGraph()
+        n0 = N.launch_count()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(self.graph, stream=s):
+                self.local = self.body()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        torch.cuda.synchronize(self.dev)
+        return N.launch_count() - n0
+
+    def step(self):
+        """One decode step: graph replay, then (N > 1) the candidate exchange and merge; returns (idx, argmax)."""
+        self.graph.replay()
+        coarse, exact, gidx = self.local
+        if self.world == 1:
+            co, ex, gi = coarse[None], exact[None], gidx[None]
+        else:
+            from fp4x_shard import gather_candidates
+            co, ex, gi = gather_candidates(coarse, exact, gidx)
+        idx, _, _, amax = self.F.head_merge(co, ex, gi, VOCAB)
+        return idx, amax
+
+    def merge_launches(self):
+        return 1
+
+
+def time_graph_class(step, name, reps=5):
+    """Average device time of one launch of a kernel class: a graph of its launches over all layers."""
+    F = step.F
+    h = step.h0
+    q = torch.empty(step.m, QKVZ, dtype=torch.bfloat16, device=step.dev).normal_()
+    o = torch.empty(step.m, HID, dtype=torch.bfloat16, device=step.dev).normal_()
+    bot = torch.empty(step.m, LR, dtype=torch.bfloat16, device=step.dev).normal_()
+
+    def run():
+        for L in step.layers:
+            if name == "nv4_qkvz":
+                F.nv4_linear(h, *L["nv4"])
+            elif name == "w6_2560x4096":
+                F.w6_linear(q[:, :W6_IN], *L["w6a"])
+            elif name == "w6_4096x2560":
+                F.w6_linear(o, *L["w6b"])
+            elif name == "w8_gate":
+                F.w8_linear(h, *L["gate"])
+            elif name == "hc_down":
+                step.fx.down(step.streams, L["qd"], L["sd"], LR, HCN)
+            elif name == "hc_up":
+                F.HCFused.up(bot, L["qi"], L["si"], step.streams, HCN, (8, 64, 8))
+
+    run()
+    torch.cuda.synchronize(step.dev)
+    s = torch.cuda.Stream(step.dev)
+    s.wait_stream(torch.cuda.current_stream(step.dev))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            run()
+    torch.cuda.current_stream(step.dev).wait_stream(s)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize(step.dev)
+    st = torch.cuda.current_stream(step.dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        g.replay()
+    e1.record(st)
+    torch.cuda.synchronize(step.dev)
+    per_launch_us = e0.elapsed_time(e1) * 1e3 / (reps * len(step.layers))
+    del g
+    return per_launch_us
+
+
+def time_head(step, reps=5):
+    """Average device time of the local fast head (coarse pass + top-512 + rescore)."""
+    h = step.h0
+    step.head.local(h)
+    torch.cuda.synchronize(step.dev)
+    s = torch.cuda.Stream(step.dev)
+    s.wait_stream(torch.cuda.current_stream(step.dev))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            step.head.local(h)
+    torch.cuda.current_stream(step.dev).wait_stream(s)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize(step.dev)
+    st = torch.cuda.current_stream(step.dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        g.replay()
+    e1.record(st)
+    torch.cuda.synchronize(step.dev)
+    del g
+    return e0.elapsed_time(e1) * 1e3 / reps
+
+
+# ----------------------------------------------------------------------------------------------------------
+# CPU oracle leg (reference arm and cpu_baseline)
+# ----------------------------------------------------------------------------------------------------------
+class CpuSample:
+    """One layer of the step plus 1/64 of the head rows (and the M x 512 rescore rows) through the numpy oracle."""
+
+    HEAD_FRACTION = 64
+
+    def __init__(self, m=3, seed=0):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import fp4x_oracle as O
+        self.O = O
+        rng = np.random.default_rng(seed)
+
+        def w(n, k):
+            return (rng.standard_normal((n, k), dtype=np.float32) * 0.02)
+
+        self.nv4 = O.quantize_nv4(w(QKVZ, HID))
+        self.w6a = O.quantize_w6(w(HID, W6_IN))
+        self.w6b = O.quantize_w6(w(W6_IN, HID))
+        self.gate = O.quantize_w8(w(GATE, HID))
+        self.qd, self.sd = O.quantize_w8(w(LR, HCN * HID))
+        self.qu, self.su = O.quantize_w8(w(HCN * HID, LR))
+        rows = VOCAB // self.HEAD_FRACTION
+        self.head_rows = rows
+        self.w8, self.s8 = O.quantize_mx8(w(rows, HID))
+        self.P, self.S = O.quantize_int2(O.mx8_dequant(self.w8, self.s8), 16)
+        self.h = O.bf16(rng.standard_normal((m, HID)).astype(np.float32))
+        self.streams = O.bf16(rng.standard_normal((m, HCN * HID)).astype(np.float32))
+        self.m = m
+        self.bytes = LAYER_BYTES + bytes_int2(rows, HID) + bytes_rescore(m, CAND, HID)
+
+    def run(self):
+        O = self.O
+        q = O.nv4_linear(self.h, *self.nv4)
+        o = O.w6_linear(O.bf16(q[:, :W6_IN]), *self.w6a)
+        O.w6_linear(O.bf16(o), *self.w6b)
+        O.w8_linear(self.h, *self.gate)
+        _, _, h = O.hc_mixer(self.streams, self.qd, self.sd, self.qu, self.su, LR, HCN)
+        O.fast_head(O.bf16(h), self.P, self.S, self.w8, self.s8, min(CAND, self.head_rows))
+
+    @staticmethod
+    def threads():
+        try:
+            from threadpoolctl import threadpool_info
+            n = [i.get("num_threads", 1) for i in threadpool_info()]
+            return max(n) if n else 1
+        except Exception:
+            return 1
+
+    def describe(self):
+        return (f"one layer of the step (NVFP4 16384x2560, W6 2560x4096, W6 4096x2560, W8 gate 512x2560, HC mixer "
+                f"512x10240 + 10240x512) + fast head on {self.head_rows} of {VOCAB} rows with the M={self.m} x 512 "
+                f"MXFP8 rescore; numpy oracle (dequantize, float64 matmul)")
+
+
+def cpu_leg(steps, warmup):
+    """Time the oracle sample: returns (GB/s, seconds per sample, sample object)."""
+    sample = CpuSample()
+    for _ in range(warmup):
+        sample.run()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        sample.run()
+    dt = (time.perf_counter() - t0) / steps
+    return sample.bytes / dt / 1e9, dt, sample
+
+
+# ----------------------------------------------------------------------------------------------------------
+# per-GEMV sweep at M = 1..16 (the first half of the metric)
+# ----------------------------------------------------------------------------------------------------------
+def gemv_sweep(device, ms=(1, 2, 4, 8, 16), reps=10):
+    import fp4x_kernels as F
+    g = torch.Generator(device=device)
+    g.manual_seed(7)
+    shapes = {
+        "mx8 16384x2560": (lambda w: F.quantize_mx8(w), lambda x, a: F.mx8_linear(x, *a), QKVZ, HID,
+                           QKVZ * HID + QKVZ * HID // 32),
+        "w8 16384x2560": (lambda w: F.quantize_w8(w), lambda x, a: F.w8_linear(x, *a), QKVZ, HID,
+                          bytes_w8(QKVZ, HID)),
+        "w6 16384x2560": (lambda w: F.quantize_w6(w), lambda x, a: F.w6_linear(x, *a), QKVZ, HID,
+                          bytes_w6(QKVZ, HID)),
+        "nv4 16384x2560": (lambda w: F.quantize_nv4(w), lambda x, a: F.nv4_linear(x, *a), QKVZ, HID,
+                           bytes_nv4(QKVZ, HID)),
+    }
+    out = {}
+    for name, (quant, call, n, k, nbytes) in shapes.items():
+        copies = max(4, int(4 * 126e6 // nbytes) + 1)  # rotate over > 4x L2 of distinct weights
+        ws = [quant(torch.randn(n, k, device=device, generator=g) * 0.02) for _ in range(copies)]
+        row = {}
+        for m in ms:
+            x = torch.randn(m, k, device=device, generator=g).to(torch.bfloat16)
+            for a in ws:
+                call(x, a)
+            torch.cuda.synchronize(device)
+            s = torch.cuda.Stream(device)
+            s.wait_stream(torch.cuda.current_stream(device))
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(gr, stream=s):
+                    for a in ws:
+                        call(x, a)
+            torch.cuda.current_stream(device).wait_stream(s)
+            gr.replay()
+            torch.cuda.synchronize(device)
+            st = torch.cuda.current_stream(device)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(st)
+            for _ in range(reps):
+                gr.replay()
+            e1.record(st)
+            torch.cuda.synchronize(device)
+            us = e0.elapsed_time(e1) * 1e3 / (reps * len(ws))
+            row[f"M={m}"] = {"us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1),
+                             "pct_of_8TBs": round(nbytes / us / 1e3 / 80.0, 1)}
+            del gr
+        out[name] = row
+        del ws
+        torch.cuda.empty_cache()
+    return out
+
+
+# ----------------------------------------------------------------------------------------------------------
+# arms
+# ----------------------------------------------------------------------------------------------------------
+def peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def traffic_for(kernel_class):
+    """DRAM bytes per launch of a kernel class from the committed ncu summary, if one exists."""
+    path = os.path.join(ROOT, "profiles", "dram_traffic.json")
+    try:
+        with open(path) as f:
+            return json.load(f).get(kernel_class)
+    except (OSError, ValueError):
+        return None
+
+
+def reference_arm(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return 0
+    gbs, dt, sample = cpu_leg(args.steps, args.warmup)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f64 (numpy oracle)", "data": "synthetic",
+        "config": {"workload": "C5 synthetic M=3 decode step, bounded CPU sample", "M": 3,
+                   "sample": sample.describe()},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": CpuSample.threads(), "kind": "port",
+                         "sample": sample.describe()},
+        "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def native_arm(args):
+    world, rank, local = dist_env()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (the CUDA path is the only path)")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    init_dist(world, local, "nccl")
+    m = args.m
+
+    step = DecodeStep(dev, m, args.layers, rank, world)
+    launches_per_step = step.capture() + step.merge_launches()
+
+    # inputs/results of the end-to-end leg: pinned host buffers
+    h_host = step.h0.cpu().pin_memory()
+    s_host = step.streams.cpu().pin_memory()
+    idx_host = torch.empty((m, CAND), dtype=torch.int32).pin_memory()
+    amax_host = torch.empty((m,), dtype=torch.int32).pin_memory()
+
+    for _ in range(args.warmup):
+        step.step()
+    torch.cuda.synchronize(dev)
+
+    st = torch.cuda.current_stream(dev)
+    clocks = ClockSampler(dev) if rank == 0 else None
+    time.sleep(0.2 if clocks else 0)
+    barrier(world, dev)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0 = time.time()
+    e0.record(st)
+    for _ in range(args.steps):
+        step.step()
+    e1.record(st)
+    torch.cuda.synchronize(dev)
+    t1 = time.time()
+    barrier(world, dev)
+    if clocks:
+        clocks.mark(t0, t1)
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world, dev)
+
+    # end to end: host inputs in, host result out, every step
+    barrier(world, dev)
+    torch.cuda.synchronize(dev)
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2.record(st)
+    for _ in range(args.steps):
+        step.h0.copy_(h_host, non_blocking=True)
+        step.streams.copy_(s_host, non_blocking=True)
+        idx, amax = step.step()
+        idx_host.copy_(idx, non_blocking=True)
+        amax_host.copy_(amax, non_blocking=True)
+    e3.record(st)
+    torch.cuda.synchronize(dev)
+    barrier(world, dev)
+    ms_e2e = max_over_ranks(e2.elapsed_time(e3) / args.steps, world, dev)
+    clk = clocks.stop() if clocks else None
+
+    step_bytes_rank = LAYER_BYTES * args.layers + head_bytes(m, step.v1 - step.v0)
+    total_bytes = step_bytes_rank * world  # equal shards (the last one holds the remainder rows)
+    value = total_bytes / (ms * 1e-3) / 1e9
+    e2e_value = total_bytes / (ms_e2e * 1e-3) / 1e9
+
+    # dominant kernel class, timed alone
+    per_class = {name: time_graph_class(step, name) for name in CLASSES}
+    head_us = time_head(step)
+    shares = {name: us * args.layers for name, us in per_class.items()}
+    shares["fast_head"] = head_us
+    top = max(shares, key=shares.get)
+    peak, peak_kind = peaks()
+    if top == "fast_head":
+        top_bytes, top_us = head_bytes(m, step.v1 - step.v0), head_us
+    else:
+        top_bytes, top_us = CLASSES[top], per_class[top]
+    achieved = top_bytes / (top_us * 1e-6) / 1e9
+
+    sweep = gemv_sweep(dev) if (world == 1 and not args.no_sweep) else None
+
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu:
+            gbs, dt, sample = cpu_leg(1, 0)
+            cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": CpuSample.threads(), "kind": "port",
+                   "sample": sample.describe() + f"; {dt:.1f} s per sample"}
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32-accumulate (f16/bf16 tensor-core products of exact weights)",
+            "data": "synthetic (seeded random-init weights, N(0,1) activations)",
+            "pct_of_8TBs": round(value / world / 80.0, 1),
+            "config": {"workload": f"C5 synthetic M={m} decode step: {args.layers} layers x (NVFP4 16384x2560, "
+                                   f"W6 2560x4096, W6 4096x2560, W8 gate 512x2560, fused HC W8 mixer) + fast LM "
+                                   f"head {VOCAB} (INT2 g16, top-512, MXFP8 rescore)",
+                       "M": m, "layers": args.layers, "cuda_graph": True,
+                       "bytes_per_step": total_bytes,
+                       "l2": "no flush: every step streams > 20x L2 of distinct weights",
+                       "parallelism": "replicas" if world == 1 else f"layer replicas + vocab-sharded head x{world}"},
+            "roofline": {"bound": "hbm", "kernel": top, "achieved": round(achieved, 1), "peak": peak,
+                         "peak_kind": f"{peak_kind} HBM copy GB/s", "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic_for(top),
+                         "per_launch_us": round(top_us, 3), "bytes_per_launch": top_bytes},
+            "class_us": {k: round(v, 2) for k, v in per_class.items()} | {"fast_head": round(head_us, 2)},
+            "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "ms_per_step": round(ms_e2e, 4),
+                    "h2d_bytes_per_step": h_host.numel() * 2 + s_host.numel() * 2,
+                    "d2h_bytes_per_step": idx_host.numel() * 4 + amax_host.numel() * 4},
+            "clocks": clk,
+            "gpu_launches": launches_per_step * args.steps,
+            "gpu_launches_per_step": launches_per_step,
+        }
+        if sweep is not None:
+            line["gemv_sweep"] = sweep
+        print(json.dumps(line), flush=True)
+    barrier(world, dev)
+    step.graph = None
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+    return 0
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("native", "reference"), default="native")
+    ap.add_argument("--m", type=int, default=3, help="tokens per step (the workload is defined at M=3)")
+    ap.add_argument("--layers", type=int, default=48)
+    ap.add_argument("--no-sweep", action="store_true", help="skip the per-GEMV M=1..16 sweep (single GPU only)")
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle baseline")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        ap.error("--warmup must be at least 3")
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != args.gpus:
+        if world == 1 and args.gpus > 1:
+            ap.error("--gpus N > 1 runs under torchrun (one process per GPU)")
+    return reference_arm(args) if args.impl == "reference" else native_arm(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -56,6 +56,11 @@ int fp4x_version(void);
 /* message describing the last failing call on this host thread ("" if none) */
 const char* fp4x_last_error_message(void);
 
+/* Diagnostic (no reference counterpart): number of kernels this library has launched, or recorded into a CUDA
+ * graph under capture, since it was loaded (all devices and threads).  Read before and after capturing a step to
+ * count the library's kernels per step. */
+int64_t fp4x_launch_count(void);
+
 /* Reads (and optionally clears) the device error word that bounded waits set when they give up.
  * Synchronizes `stream`.  Returns FP4X_OK when the word is zero, FP4X_ERR_DEVICE otherwise. */
 int fp4x_device_error(void* stream, int clear, int* code_out);

@@ -13,6 +13,7 @@
 namespace fp4x {
 
 __device__ int g_dev_error = 0;
+std::atomic<int64_t> g_launches{0};
 
 int* dev_error_ptr() {
   static int* ptrs[64] = {};
@@ -436,6 +437,8 @@ extern "C" {
 int fp4x_version(void) { return 200; }
 
 const char* fp4x_last_error_message(void) { return t_msg.c_str(); }
+
+int64_t fp4x_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 int fp4x_device_error(void* stream, int clear, int* code_out) {
   int v = 0;

@@ -3,6 +3,7 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
 #include <string>
 
 #include "fp4x.h"
@@ -20,6 +21,9 @@ struct DeviceFacts {
 };
 const DeviceFacts& device_facts();
 
+// kernels launched (or recorded into a graph under capture) by this library; read by fp4x_launch_count
+extern std::atomic<int64_t> g_launches;
+
 // launch with programmatic stream serialization (the kernel may begin while its predecessor drains)
 template <typename Kernel, typename... Args>
 cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, Args... args) {
@@ -33,7 +37,9 @@ cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaSt
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kernel, args...);
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (e == cudaSuccess) g_launches.fetch_add(1, std::memory_order_relaxed);
+  return e;
 }
 
 // address of the device error word on the current device (cudaGetSymbolAddress, cached per device)

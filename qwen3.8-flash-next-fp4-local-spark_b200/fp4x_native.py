@@ -38,6 +38,7 @@ class W8Item(ctypes.Structure):
 _SIGS = {
     "fp4x_version": ([], _i32),
     "fp4x_last_error_message": ([], ctypes.c_char_p),
+    "fp4x_launch_count": ([], _i64),
     "fp4x_device_error": ([_p, _i32, ctypes.POINTER(ctypes.c_int)], _i32),
     "fp4x_gemv_query": ([_i32, _i64, _i64, _i64, _i64, _i32, ctypes.POINTER(_sz), ctypes.POINTER(_i64)], _i32),
     "fp4x_plan_describe": ([_i32, _i64, _i64, _i64, _i64, _i32, _i32, ctypes.c_char_p, _sz], _i32),
@@ -182,6 +183,11 @@ def plan(fmt, m, n, k, batch=1, group=16, whole=False):
     buf = ctypes.create_string_buffer(512)
     call("fp4x_plan_describe", fmt, m, n, k, batch, group, 1 if whole else 0, buf, 512)
     return buf.value.decode()
+
+
+def launch_count():
+    """Kernels the library has launched (or recorded into a graph under capture) since it was loaded."""
+    return int(lib().fp4x_launch_count())
 
 
 def device_error(clear=True, device=None):
