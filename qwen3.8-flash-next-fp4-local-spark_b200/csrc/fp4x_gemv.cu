@@ -635,3 +635,81 @@ int fp4x_hc_mixer_unfused(const void* x, int64_t x_stride, const void* qd, const
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------------------
+// MXFP8 GEMV without caller scratch: split-K partials and arrival counters live in file-scope static device
+// arrays of the library (one copy per device).  The counters are zero when the module loads and every completed
+// call leaves them zero; the partial tiles are written before they are read.
+// ------------------------------------------------------------------------------------------------------
+namespace fp4x {
+
+constexpr size_t kStaticWsBytes = size_t(8) << 20;  // 8 MiB of split-K partial tiles
+constexpr int64_t kStaticCounters = 32768;          // int32 arrival counters (rows up to 524,288)
+
+static __device__ __align__(256) unsigned char g_static_ws[kStaticWsBytes];
+static __device__ __align__(256) int32_t g_static_counters[kStaticCounters];
+
+// device addresses of the static scratch on the current device, resolved on the first call per device
+static int static_scratch(void** ws, int32_t** counters) {
+  static void* ws_of[64] = {};
+  static int32_t* cnt_of[64] = {};
+  static std::mutex mu;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return fail(FP4X_ERR_CUDA, std::string("cudaGetDevice: ") + cudaGetErrorString(e));
+  if (dev < 0 || dev >= 64) return fail(FP4X_ERR_UNSUPPORTED, "device ordinal above 63");
+  std::lock_guard<std::mutex> lk(mu);
+  if (!ws_of[dev]) {
+    void* w = nullptr;
+    void* c = nullptr;
+    e = cudaGetSymbolAddress(&w, g_static_ws);
+    if (e != cudaSuccess)
+      return fail(FP4X_ERR_CUDA, std::string("cudaGetSymbolAddress(static workspace): ") + cudaGetErrorString(e));
+    e = cudaGetSymbolAddress(&c, g_static_counters);
+    if (e != cudaSuccess)
+      return fail(FP4X_ERR_CUDA, std::string("cudaGetSymbolAddress(static counters): ") + cudaGetErrorString(e));
+    ws_of[dev] = w;
+    cnt_of[dev] = (int32_t*)c;
+  }
+  *ws = ws_of[dev];
+  *counters = cnt_of[dev];
+  return FP4X_OK;
+}
+
+}  // namespace fp4x
+
+extern "C" int fp4x_mx8_linear_noalloc(const void* x, int64_t x_stride, const void* w, const void* s, void* out,
+                                       int64_t out_stride, int out_dtype, int64_t m, int64_t n, int64_t k,
+                                       void* stream) {
+  int rc;
+  if ((rc = check_out_dtype(out_dtype))) return rc;
+  Plan pl;
+  if ((rc = make_plan(FMT_MX8, m, n, k, 1, 16, kStreamK, 0, pl))) return rc;
+  if (pl.ws_bytes > kStaticWsBytes || pl.counters > kStaticCounters)
+    return fail(FP4X_ERR_WORKSPACE, "fp4x_mx8_linear_noalloc: this shape needs " + std::to_string(pl.ws_bytes) +
+                                        " workspace bytes and " + std::to_string(pl.counters) +
+                                        " counters; the static scratch holds " + std::to_string(kStaticWsBytes) +
+                                        " bytes and " + std::to_string(kStaticCounters) + " counters");
+  if ((rc = check_x(x, x_stride, k))) return rc;
+  if ((rc = check_rows(w, k, "weight"))) return rc;
+  if (!s) return fail(FP4X_ERR_INVALID_ARG, "null scales");
+  const int64_t lds = k / 32;
+  const int scw = scale_width(s, lds, pl.SB);
+  if (!scw) return fail(FP4X_ERR_UNSUPPORTED, "scale rows must be 4-byte aligned");
+  if (!out) return fail(FP4X_ERR_INVALID_ARG, "null output");
+  if (out_stride < n) return fail(FP4X_ERR_INVALID_ARG, "out_stride < n");
+  void* ws = nullptr;
+  int32_t* counters = nullptr;
+  if ((rc = static_scratch(&ws, &counters))) return rc;
+  GemvArgs a;
+  std::memset(&a, 0, sizeof(a));
+  if ((rc = encode_rows_uncached(&a.tm0, w, n, k, pl.BI0))) return rc;
+  a.item = GemvItem{x, (const uint8_t*)s, out, nullptr};
+  a.batch = nullptr;
+  a.M = (int)m; a.N = (int)n; a.K = (int)k;
+  a.x_stride = x_stride; a.lds = lds; a.scw = scw;
+  a.out_stride = out_stride; a.out_dtype = out_dtype; a.post = 1.f; a.group = 16;
+  a.ws = (float*)ws; a.sem = counters;
+  fill_args(pl, a);
+  return launch_nt<FMT_MX8, EPI_STORE>(pl, a, 1, (cudaStream_t)stream);
+}

@@ -43,6 +43,7 @@ _SIGS = {
     "fp4x_gemv_query": ([_i32, _i64, _i64, _i64, _i64, _i32, ctypes.POINTER(_sz), ctypes.POINTER(_i64)], _i32),
     "fp4x_plan_describe": ([_i32, _i64, _i64, _i64, _i64, _i32, _i32, ctypes.c_char_p, _sz], _i32),
     "fp4x_mx8_linear": ([_p, _i64, _p, _p, _p, _i64, _i32, _i64, _i64, _i64, _p, _sz, _p, _i64, _p], _i32),
+    "fp4x_mx8_linear_noalloc": ([_p, _i64, _p, _p, _p, _i64, _i32, _i64, _i64, _i64, _p], _i32),
     "fp4x_bf16_linear": ([_p, _i64, _p, _p, _i64, _i32, _i64, _i64, _i64, _p, _sz, _p, _i64, _p], _i32),
     "fp4x_nv4_linear": ([_p, _i64, _p, _p, _f32, _p, _i64, _i32, _i64, _i64, _i64, _p, _sz, _p, _i64, _p], _i32),
     "fp4x_w8_linear": ([_p, _i64, _p, _p, _p, _i64, _i32, _i64, _i64, _i64, _p, _sz, _p, _i64, _p], _i32),
