@@ -114,6 +114,13 @@ __host__ __device__ inline int64_t range_begin(int64_t U, int W, int w) { return
 // the part that owns unit u when U units are split over W parts by range_begin
 __host__ __device__ inline int owner_of(int64_t u, int64_t U, int W) { return (int)(((u + 1) * W + U - 1) / U) - 1; }
 
+// fetch-and-add with acquire-release semantics at GPU scope
+FP4X_DEV int atomic_add_acq_rel(int* p, int v) {
+  int old;
+  asm volatile("atom.acq_rel.gpu.add.s32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+
 // ------------------------------------------------------------------------------------------------------
 // TMA, async copies, ldmatrix
 // ------------------------------------------------------------------------------------------------------
@@ -240,13 +247,15 @@ FP4X_DEV void stage_activations(const GemvArgs& A, const GemvItem& it, uint8_t* 
     }
     named_bar(1, nthr);
   }
+  // Only the M real token rows are converted: B columns >= M are never written, and since each column of an MMA
+  // result depends on its own B column alone, whatever they hold reaches only output columns that are not stored.
   const uint32_t xbase = smem_u32(base + A.smem_x);
   const int nblk = KPW / G.qb;
-  for (int idx = tid; idx < MP * nblk; idx += nthr) {
-    const int tok = idx / nblk, kb = idx - tok * nblk;
+  for (int tok = 0; tok < A.M; ++tok)
+  for (int kb = tid; kb < nblk; kb += nthr) {
     const float scl = G.xf16 ? xsc[tok] : 1.f;
     uint32_t v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-    if (tok < A.M) {
+    {
       const __nv_bfloat16* src = xr + (int64_t)tok * KPW + kb * G.qb;
       if (G.qb == 4) {
         const uint2 t = *reinterpret_cast<const uint2*>(src);
@@ -795,13 +804,12 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
     const int scw = A.scw;
     const int words_per_row = G.sn ? A.SB / scw : 0;
     const int sd = FMT == FMT_INT2 ? A.group / 2 : G.sd;
+    int s = 0, round = 0;
+    int blk = (int)(u_begin / A.NCH), chunk = (int)(u_begin - (int64_t)blk * A.NCH);
     for (int64_t q = 0; q < nunits; ++q) {
-      const int s = (int)(q % A.NS);
-      if (q >= A.NS) {
-        if (!mbar_wait_bounded(empty0 + 8 * s, (uint32_t)(((q / A.NS) - 1) & 1), A.err)) break;
+      if (round > 0) {
+        if (!mbar_wait_bounded(empty0 + 8 * s, (uint32_t)((round - 1) & 1), A.err)) break;
       }
-      const int64_t u = u_begin + q;
-      const int blk = (int)(u / A.NCH), chunk = (int)(u - (int64_t)blk * A.NCH);
       const int k0 = k_panel0 + chunk * A.KC;
       const uint32_t stage = smem_u32(base) + (uint32_t)s * A.STG;
       const uint32_t bar = full0 + 8 * s;
@@ -826,6 +834,8 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
         }
       }
       cp_async_arrive_noinc(bar);
+      if (++s == A.NS) { s = 0; ++round; }
+      if (++chunk == A.NCH) { chunk = 0; ++blk; }
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
     return;
@@ -896,14 +906,15 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
       __stcg(reinterpret_cast<float2*>(mine + g * MP + m), make_float2(acc[t][0], acc[t][1]));
       __stcg(reinterpret_cast<float2*>(mine + (g + 8) * MP + m), make_float2(acc[t][2], acc[t][3]));
     }
-    __threadfence();
+    // The warp barrier orders every lane's partial stores before lane 0's release; the acquire half of the same
+    // atomic, followed by the warp barrier, orders the last arriver's reads of the other partials after it.
     __syncwarp();
     int* semp = A.sem + ((int64_t)b * A.RT + blk) * kCWarps + warp;
     int last = 0;
-    if (lane == 0) last = (atomicAdd(semp, 1) == A.KP * segs - 1);
+    if (lane == 0) last = (atomic_add_acq_rel(semp, 1) == A.KP * segs - 1);
     last = __shfl_sync(0xffffffffu, last, 0);
+    __syncwarp();
     if (!last) return;
-    __threadfence();
     float tot[NT][4];
     zero4<NT>(tot);
     for (int pp = 0; pp < A.KP; ++pp)
@@ -921,16 +932,16 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
     if (lane == 0) atomicExch(semp, 0);
   };
 
+  int s = 0;
+  uint32_t phase = 0;
+  int blk = (int)(u_begin / A.NCH), chunk = (int)(u_begin - (int64_t)blk * A.NCH);
   for (int64_t q = 0; q < nunits; ++q) {
-    const int s = (int)(q % A.NS);
-    const int64_t u = u_begin + q;
-    const int blk = (int)(u / A.NCH), chunk = (int)(u - (int64_t)blk * A.NCH);
     if (blk != cur) {
       if (cur >= 0) flush(cur);
       zero4<NT>(acc);
       cur = blk;
     }
-    if (!mbar_wait_bounded(full0 + 8 * s, (uint32_t)((q / A.NS) & 1), A.err)) { ok = false; break; }
+    if (!mbar_wait_bounded(full0 + 8 * s, phase, A.err)) { ok = false; break; }
     const uint32_t stage = smem_u32(base) + (uint32_t)s * A.STG;
     wc.p0 = stage;
     wc.p1 = stage + A.off_p1;
@@ -939,6 +950,8 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
     compute_stage<FMT, NT>(wc, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * s);
+    if (++s == A.NS) { s = 0; phase ^= 1u; }
+    if (++chunk == A.NCH) { chunk = 0; ++blk; }
   }
   if (ok && cur >= 0) flush(cur);
 }
