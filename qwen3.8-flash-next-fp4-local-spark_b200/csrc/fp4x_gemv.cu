@@ -154,7 +154,7 @@ struct Plan {
   int NT, MP;
   int KPW, KP, KC, NCH, CPP, RT, NS, SMAX, whole;
   int BI0, BI1, NB0, SB, STG, off_p1, off_sc, XP;
-  int smem_x, smem_misc, smem_scr, smem_xraw, smem_total;
+  int smem_x, smem_misc, smem_scr, smem_xraw, smem_comb, smem_total;
   size_t ws_bytes;
   int64_t counters;
 };
@@ -207,7 +207,8 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
   const int sd = fmt == FMT_INT2 ? group / 2 : G.sd;
   const double wbytes = (double)batch * N * K * bytes_per_k(fmt, group);
   const int misc = 512;
-  const int scr_bytes = epi_scratch ? kCWarps * 16 * pl.MP * 4 : 0;
+  const int scr_bytes = epi_scratch ? kRW * 16 * pl.MP * 4 : 0;
+  const int comb_bytes = kRW * 32 * pl.NT * 4 * 4;
   const int cap1 = dv.smem_optin;
   const int cap2 = dv.smem_sm / 2 - 2048;  // two CTAs per SM (1 KB reserved per CTA, 1 KB alignment slack)
 
@@ -234,7 +235,7 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
     c.STG = round_up(c.off_sc + kRB * c.SB, 1024);
     c.XP = (kpw / 16) * 32 + 32;
     const int xbytes = round_up(c.MP * c.XP, 16) + (int)M * kpw * 2;  // permuted panel + raw bf16 panel
-    const int fixed = xbytes + misc + scr_bytes + 1024;
+    const int fixed = xbytes + misc + scr_bytes + comb_bytes + 1024;
     for (int cps = 2; cps >= 1; --cps) {
       const int cap = cps == 2 ? cap2 : cap1;
       int ns = (cap - fixed) / c.STG;
@@ -270,10 +271,11 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
   pl.smem_misc = pl.smem_x + round_up(pl.MP * pl.XP, 16);
   pl.smem_scr = pl.smem_misc + misc;
   pl.smem_xraw = pl.smem_scr + round_up(scr_bytes, 16);
-  pl.smem_total = pl.smem_xraw + (int)M * pl.KPW * 2 + 1024;
+  pl.smem_comb = pl.smem_xraw + round_up((int)M * pl.KPW * 2, 16);
+  pl.smem_total = pl.smem_comb + comb_bytes + 1024;
   pl.SMAX = whole ? 1 : (int)((int64_t)(pl.NCH - 1) * pl.CPP / Up) + 2;
   if (pl.SMAX > pl.CPP) pl.SMAX = pl.CPP;
-  const size_t slot = (size_t)kCWarps * 16 * pl.MP * sizeof(float);
+  const size_t slot = (size_t)kRW * 16 * pl.MP * sizeof(float);
   const bool split = !whole && pl.NCH > 1;
   if (pl.KP > 1)
     pl.ws_bytes = (size_t)batch * pl.KP * pl.RT * pl.SMAX * slot;
@@ -281,7 +283,7 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
     pl.ws_bytes = (size_t)batch * pl.CPP * 2 * slot;
   else
     pl.ws_bytes = 0;
-  pl.counters = (pl.KP > 1 || split) ? (int64_t)batch * pl.RT * kCWarps : 0;
+  pl.counters = (pl.KP > 1 || split) ? (int64_t)batch * pl.RT * kRW : 0;
   return FP4X_OK;
 }
 
@@ -309,6 +311,7 @@ static void fill_args(const Plan& pl, GemvArgs& a) {
   a.BI0 = pl.BI0; a.BI1 = pl.BI1; a.NB0 = pl.NB0; a.SB = pl.SB; a.STG = pl.STG;
   a.off_p1 = pl.off_p1; a.off_sc = pl.off_sc; a.XP = pl.XP;
   a.smem_x = pl.smem_x; a.smem_misc = pl.smem_misc; a.smem_scr = pl.smem_scr; a.smem_xraw = pl.smem_xraw;
+  a.smem_comb = pl.smem_comb;
 }
 
 // widest cp.async (16/8/4 bytes) that keeps every scale copy aligned

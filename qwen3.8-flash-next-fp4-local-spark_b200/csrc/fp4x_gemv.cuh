@@ -27,9 +27,11 @@
 
 namespace fp4x {
 
-constexpr int kCWarps = 4;                       // consumer warps
+constexpr int kRW = 4;                           // row warps: 16 rows each, one 64-row block
+constexpr int kKG = 2;                           // k-groups: each stage's chunks are split between two warp sets
+constexpr int kCWarps = kRW * kKG;               // consumer warps
 constexpr int kThreads = (kCWarps + 1) * 32;     // + one producer warp
-constexpr int kRB = 16 * kCWarps;                // rows per stage
+constexpr int kRB = 16 * kRW;                    // rows per stage
 constexpr int kMaxStages = 8;
 
 enum Fmt : int { FMT_MX8 = 0, FMT_W8 = 1, FMT_W6 = 2, FMT_NV4 = 3, FMT_BF16 = 4, FMT_INT2 = 5 };
@@ -99,6 +101,7 @@ struct alignas(64) GemvArgs {
   int XP;                 // activation token pitch (bytes)
   int smem_x, smem_misc, smem_scr;  // offsets of the regions after the 1024-aligned base (stages start at 0)
   int smem_xraw;          // raw bf16 activation panel [M][KPW] (bulk-copied after griddepcontrol.wait)
+  int smem_comb;          // k-group hand-over of partial sums: [kRW][32 lanes][NT * 4] fp32
   int lr, hc, bj;         // hyper-connection epilogues
   const void* nrm;        // HC up: normalized input [M, hc*H]
   int64_t nrm_stride;
@@ -305,7 +308,7 @@ FP4X_DEV void stage_activations(const GemvArgs& A, const GemvItem& it, uint8_t* 
 // ------------------------------------------------------------------------------------------------------
 struct WarpCtx {
   uint32_t p0, p1, sc;  // shared addresses of the stage planes and scales
-  int BI0, BI1, NB0, SB;
+  int BI0, BI1, NB0, SB, CPB;
   uint32_t lrow0;       // ldmatrix: this lane's row offset inside a box (row * BI0)
   int lswz, lsel;       // ldmatrix: this lane's swizzle key and chunk select (0/1)
   uint32_t xb;          // activation address of step 0 of this stage for token row g and tq
@@ -368,10 +371,11 @@ FP4X_DEV void mma_bf16_acc(float (&d)[NT][4], const uint32_t (&a)[4], const uint
   for (int t = 0; t < NT; ++t) mma_bf16(d[t], a, b0[t], b1[t], d[t]);
 }
 
-// The stage functions below are fully unrolled over a compile-time stage shape (CPB 16-byte chunks per box: 8 for
-// 128-byte boxes, 4 for 64-byte boxes; NB boxes per stage).  Every shared-memory load of a box (ldmatrix
-// fragments, activation fragments, scales) is issued before the arithmetic that consumes it, so the load latencies
-// overlap, and formats that chain MMAs spread them over independent accumulators.
+// A stage holds NB0 boxes of CPB 16-byte chunks (CPB = 8 for 128-byte boxes, 4 for 64-byte boxes) of 64 rows.
+// The two k-groups of consumer warps split it: each processes NCHK consecutive chunks of one box (box b, first
+// chunk c0).  The stage functions are fully unrolled over NCHK; every shared-memory load of the range (ldmatrix
+// fragments, activation fragments, scales) is issued before the arithmetic that consumes it, and formats that chain
+// MMAs spread them over independent accumulators.
 
 template <int NT, int NACC>
 FP4X_DEV void zero_accs(float (&a)[NACC][NT][4]) {
@@ -391,22 +395,27 @@ FP4X_DEV void fold_accs(float (&acc)[NT][4], const float (&a)[NACC][NT][4]) {
     }
 }
 
+// NB consecutive scale bytes (NB = 1, 2 or 4; the address is NB-aligned) in the low bytes of a word
+template <int NB>
+FP4X_DEV uint32_t ld_bytes(uint32_t addr) {
+  if (NB == 4) return lds32(addr);
+  if (NB == 2) return lds16(addr);
+  return lds8(addr);
+}
+
 // MXFP8: a chunk pair is one 32-group G; steps 2G + h; group scales applied to the fp32 group sums
-template <int NT, int CPB, int NB>
-FP4X_DEV void stage_mx8(const WarpCtx& c, float (&acc)[NT][4]) {
-  constexpr int GPB = CPB / 2, NG = NB * GPB, NW = (NG + 3) / 4;
+template <int NT, int NCHK>
+FP4X_DEV void stage_mx8(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) {
+  constexpr int NG = NCHK / 2;
+  const int G0 = (b * c.CPB + c0) >> 1;
   uint32_t r[NG][4];
   uint32_t b0[2 * NG][NT], b1[2 * NG][NT];
-  uint32_t slo[NW], shi[NW];
 #pragma unroll
-  for (int j = 0; j < NG; ++j) ld_pair(c, j / GPB, 2 * (j % GPB), r[j][0], r[j][1], r[j][2], r[j][3]);
+  for (int j = 0; j < NG; ++j) ld_pair(c, b, c0 + 2 * j, r[j][0], r[j][1], r[j][2], r[j][3]);
 #pragma unroll
-  for (int s = 0; s < 2 * NG; ++s) load_b<NT>(c, s, b0[s], b1[s]);
-#pragma unroll
-  for (int i = 0; i < NW; ++i) {
-    slo[i] = lds32(c.sc + (c.rbase + c.g) * c.SB + 4 * i);
-    shi[i] = lds32(c.sc + (c.rbase + c.g + 8) * c.SB + 4 * i);
-  }
+  for (int s = 0; s < 2 * NG; ++s) load_b<NT>(c, 2 * G0 + s, b0[s], b1[s]);
+  const uint32_t slo = ld_bytes<NG>(c.sc + (c.rbase + c.g) * c.SB + G0);
+  const uint32_t shi = ld_bytes<NG>(c.sc + (c.rbase + c.g + 8) * c.SB + G0);
 #pragma unroll
   for (int j = 0; j < NG; ++j) {
     float tmp[NT][4];
@@ -416,8 +425,8 @@ FP4X_DEV void stage_mx8(const WarpCtx& c, float (&acc)[NT][4]) {
     const uint32_t A1[4] = {e4m3x2_to_f16x2(r[j][2]), e4m3x2_to_f16x2(r[j][3]), e4m3x2_to_f16x2(r[j][2] >> 16),
                             e4m3x2_to_f16x2(r[j][3] >> 16)};
     mma_f16_acc<NT>(tmp, A1, b0[2 * j + 1], b1[2 * j + 1], false);
-    const float sl = e8m0_to_f32((slo[j >> 2] >> (8 * (j & 3))) & 0xffu);
-    const float sh = e8m0_to_f32((shi[j >> 2] >> (8 * (j & 3))) & 0xffu);
+    const float sl = e8m0_to_f32((slo >> (8 * j)) & 0xffu);
+    const float sh = e8m0_to_f32((shi >> (8 * j)) & 0xffu);
     fma_scaled<NT>(acc, tmp, sl, sh);
   }
 }
@@ -426,23 +435,24 @@ FP4X_DEV uint32_t w8_pair_lo(uint32_t w) { return hadd2(prmt(w ^ 0x80808080u, 0x
 FP4X_DEV uint32_t w8_pair_hi(uint32_t w) { return hadd2(prmt(w ^ 0x80808080u, 0x64646464u, 0x4342u), 0xE480E480u); }
 
 // W8: four chunks per 64-group G; steps 4G + h
-template <int NT, int CPB, int NB>
-FP4X_DEV void stage_w8(const WarpCtx& c, float (&acc)[NT][4]) {
-  constexpr int GPB = CPB / 4, NG = NB * GPB;
+template <int NT, int NCHK>
+FP4X_DEV void stage_w8(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) {
+  constexpr int NG = NCHK / 4;
+  const int G0 = (b * c.CPB + c0) >> 2;
   uint32_t r[NG][8];
   uint32_t b0[4 * NG][NT], b1[4 * NG][NT];
   float slo[NG], shi[NG];
 #pragma unroll
   for (int j = 0; j < NG; ++j) {
-    ld_pair(c, j / GPB, 4 * (j % GPB), r[j][0], r[j][1], r[j][2], r[j][3]);
-    ld_pair(c, j / GPB, 4 * (j % GPB) + 2, r[j][4], r[j][5], r[j][6], r[j][7]);
+    ld_pair(c, b, c0 + 4 * j, r[j][0], r[j][1], r[j][2], r[j][3]);
+    ld_pair(c, b, c0 + 4 * j + 2, r[j][4], r[j][5], r[j][6], r[j][7]);
   }
 #pragma unroll
-  for (int s = 0; s < 4 * NG; ++s) load_b<NT>(c, s, b0[s], b1[s]);
+  for (int s = 0; s < 4 * NG; ++s) load_b<NT>(c, 4 * G0 + s, b0[s], b1[s]);
 #pragma unroll
   for (int j = 0; j < NG; ++j) {
-    slo[j] = __uint_as_float(lds32(c.sc + (c.rbase + c.g) * c.SB + 4 * j));
-    shi[j] = __uint_as_float(lds32(c.sc + (c.rbase + c.g + 8) * c.SB + 4 * j));
+    slo[j] = __uint_as_float(lds32(c.sc + (c.rbase + c.g) * c.SB + 4 * (G0 + j)));
+    shi[j] = __uint_as_float(lds32(c.sc + (c.rbase + c.g + 8) * c.SB + 4 * (G0 + j)));
   }
 #pragma unroll
   for (int j = 0; j < NG; ++j) {
@@ -461,119 +471,113 @@ FP4X_DEV uint32_t w6_lane(uint32_t lo_src, uint32_t hi_src) {
   return (lo_src & 0x000F000Fu) | (hi_src & 0x00300030u) | 0x64006400u;
 }
 
-// W6: a chunk of the low-nibble plane is one 32-group G (thread: 8 k = 32G + 8tq + r); steps 2G + h.
-// Processed one box (CPB groups) at a time.
-template <int NT, int CPB, int NB>
-FP4X_DEV void stage_w6(const WarpCtx& c, float (&acc)[NT][4]) {
+// W6: a chunk of the low-nibble plane is one 32-group G (thread: 8 k = 32G + 8tq + r); steps 2G + h
+template <int NT, int NCHK>
+FP4X_DEV void stage_w6(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) {
   const uint32_t kNeg1056 = 0xE420E420u;
+  const int G0 = b * c.CPB + c0;
+  uint32_t r[NCHK / 2][4];
+  uint32_t hs[NCHK][2];
+  uint32_t b0[2 * NCHK][NT], b1[2 * NCHK][NT];
+  uint32_t sw[2][NCHK / 2];
 #pragma unroll
-  for (int b = 0; b < NB; ++b) {
-    uint32_t r[CPB / 2][4];
-    uint32_t hs[CPB][2];
-    uint32_t b0[2 * CPB][NT], b1[2 * CPB][NT];
-    uint32_t sw[2][CPB / 2];
+  for (int u = 0; u < NCHK / 2; ++u) ld_pair(c, b, c0 + 2 * u, r[u][0], r[u][1], r[u][2], r[u][3]);
 #pragma unroll
-    for (int u = 0; u < CPB / 2; ++u) ld_pair(c, b, 2 * u, r[u][0], r[u][1], r[u][2], r[u][3]);
+  for (int gg = 0; gg < NCHK; ++gg)
 #pragma unroll
-    for (int gg = 0; gg < CPB; ++gg) {
-      const int G = b * CPB + gg;
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const int row = c.rbase + c.g + 8 * q;
-        hs[gg][q] = lds16(c.p1 + swz((uint32_t)(row * c.BI1 + 8 * G + 2 * c.tq), c.BI1));
-      }
+    for (int q = 0; q < 2; ++q) {
+      const int row = c.rbase + c.g + 8 * q;
+      hs[gg][q] = lds16(c.p1 + swz((uint32_t)(row * c.BI1 + 8 * (G0 + gg) + 2 * c.tq), c.BI1));
     }
 #pragma unroll
-    for (int s = 0; s < 2 * CPB; ++s) load_b<NT>(c, 2 * b * CPB + s, b0[s], b1[s]);
+  for (int s = 0; s < 2 * NCHK; ++s) load_b<NT>(c, 2 * G0 + s, b0[s], b1[s]);
 #pragma unroll
-    for (int i = 0; i < CPB / 2; ++i) {
-      sw[0][i] = lds32(c.sc + (c.rbase + c.g) * c.SB + 2 * b * CPB + 4 * i);
-      sw[1][i] = lds32(c.sc + (c.rbase + c.g + 8) * c.SB + 2 * b * CPB + 4 * i);
+  for (int i = 0; i < NCHK / 2; ++i) {
+    sw[0][i] = lds32(c.sc + (c.rbase + c.g) * c.SB + 2 * G0 + 4 * i);
+    sw[1][i] = lds32(c.sc + (c.rbase + c.g + 8) * c.SB + 2 * G0 + 4 * i);
+  }
+#pragma unroll
+  for (int gg = 0; gg < NCHK; ++gg) {
+    uint32_t L[2], Hs[2];
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      L[q] = r[gg >> 1][2 * (gg & 1) + q];
+      Hs[q] = prmt(hs[gg][q], 0u, 0x4140u);
     }
+    float tmp[NT][4];
 #pragma unroll
-    for (int gg = 0; gg < CPB; ++gg) {
-      uint32_t L[2], Hs[2];
+    for (int h = 0; h < 2; ++h) {
+      uint32_t A[4];
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
-        L[q] = r[gg >> 1][2 * (gg & 1) + q];
-        Hs[q] = prmt(hs[gg][q], 0u, 0x4140u);
-      }
-      float tmp[NT][4];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t A[4];
-#pragma unroll
-        for (int q = 0; q < 2; ++q) {
-          uint32_t lo, hi;
-          if (h == 0) {
-            lo = w6_lane(L[q], Hs[q] << 4);         // elements r0, r4
-            hi = w6_lane(L[q] >> 4, Hs[q]);         // r1, r5
-          } else {
-            lo = w6_lane(L[q] >> 8, Hs[q] << 2);    // r2, r6
-            hi = w6_lane(L[q] >> 12, Hs[q] >> 2);   // r3, r7
-          }
-          A[q] = hadd2(lo, kNeg1056);
-          A[2 + q] = hadd2(hi, kNeg1056);
+        uint32_t lo, hi;
+        if (h == 0) {
+          lo = w6_lane(L[q], Hs[q] << 4);         // elements r0, r4
+          hi = w6_lane(L[q] >> 4, Hs[q]);         // r1, r5
+        } else {
+          lo = w6_lane(L[q] >> 8, Hs[q] << 2);    // r2, r6
+          hi = w6_lane(L[q] >> 12, Hs[q] >> 2);   // r3, r7
         }
-        mma_f16_acc<NT>(tmp, A, b0[2 * gg + h], b1[2 * gg + h], h == 0);
+        A[q] = hadd2(lo, kNeg1056);
+        A[2 + q] = hadd2(hi, kNeg1056);
       }
-      const float sl = f16_bits_to_f32((sw[0][gg >> 1] >> (16 * (gg & 1))) & 0xffffu);
-      const float sh = f16_bits_to_f32((sw[1][gg >> 1] >> (16 * (gg & 1))) & 0xffffu);
-      fma_scaled<NT>(acc, tmp, sl, sh);
+      mma_f16_acc<NT>(tmp, A, b0[2 * gg + h], b1[2 * gg + h], h == 0);
     }
+    const float sl = f16_bits_to_f32((sw[0][gg >> 1] >> (16 * (gg & 1))) & 0xffffu);
+    const float sh = f16_bits_to_f32((sw[1][gg >> 1] >> (16 * (gg & 1))) & 0xffffu);
+    fma_scaled<NT>(acc, tmp, sl, sh);
   }
 }
 
 // NVFP4: a chunk C is 32 k = two 16-groups (thread: k = 32C + 8tq + 4h + i, group 2C + tq/2); steps 2C + h.
 // The e4m3 block scale multiplies the e2m1 values in f16 (exact: <= 6 significant bits, normal range).
-template <int NT, int CPB, int NB>
-FP4X_DEV void stage_nv4(const WarpCtx& c, float (&acc)[NT][4]) {
+template <int NT, int NCHK>
+FP4X_DEV void stage_nv4(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) {
   constexpr int NACC = 4;
+  const int C0 = b * c.CPB + c0;
+  uint32_t r[NCHK / 2][4];
+  uint32_t b0[2 * NCHK][NT], b1[2 * NCHK][NT];
+  uint32_t sc8[NCHK][2];
 #pragma unroll
-  for (int b = 0; b < NB; ++b) {
-    uint32_t r[CPB / 2][4];
-    uint32_t b0[2 * CPB][NT], b1[2 * CPB][NT];
-    uint32_t sc8[CPB][2];
+  for (int u = 0; u < NCHK / 2; ++u) ld_pair(c, b, c0 + 2 * u, r[u][0], r[u][1], r[u][2], r[u][3]);
 #pragma unroll
-    for (int u = 0; u < CPB / 2; ++u) ld_pair(c, b, 2 * u, r[u][0], r[u][1], r[u][2], r[u][3]);
+  for (int s = 0; s < 2 * NCHK; ++s) load_b<NT>(c, 2 * C0 + s, b0[s], b1[s]);
 #pragma unroll
-    for (int s = 0; s < 2 * CPB; ++s) load_b<NT>(c, 2 * b * CPB + s, b0[s], b1[s]);
-#pragma unroll
-    for (int cc = 0; cc < CPB; ++cc) {
-      const int grp = 2 * (b * CPB + cc) + (c.tq >> 1);
-      sc8[cc][0] = lds8(c.sc + (c.rbase + c.g) * c.SB + grp);
-      sc8[cc][1] = lds8(c.sc + (c.rbase + c.g + 8) * c.SB + grp);
-    }
-    float accs[NACC][NT][4];
-    zero_accs<NT, NACC>(accs);
-#pragma unroll
-    for (int cc = 0; cc < CPB; ++cc) {
-      const uint32_t s2lo = prmt(e4m3x2_to_f16x2(sc8[cc][0]), 0u, 0x1010u);
-      const uint32_t s2hi = prmt(e4m3x2_to_f16x2(sc8[cc][1]), 0u, 0x1010u);
-      const uint32_t wlo = r[cc >> 1][2 * (cc & 1)], whi = r[cc >> 1][2 * (cc & 1) + 1];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const uint32_t A[4] = {hmul2(e2m1x2_to_f16x2(wlo >> (16 * h)), s2lo),
-                               hmul2(e2m1x2_to_f16x2(whi >> (16 * h)), s2hi),
-                               hmul2(e2m1x2_to_f16x2(wlo >> (16 * h + 8)), s2lo),
-                               hmul2(e2m1x2_to_f16x2(whi >> (16 * h + 8)), s2hi)};
-        mma_f16_acc<NT>(accs[(2 * cc + h) % NACC], A, b0[2 * cc + h], b1[2 * cc + h], false);
-      }
-    }
-    fold_accs<NT, NACC>(acc, accs);
+  for (int cc = 0; cc < NCHK; ++cc) {
+    const int grp = 2 * (C0 + cc) + (c.tq >> 1);
+    sc8[cc][0] = lds8(c.sc + (c.rbase + c.g) * c.SB + grp);
+    sc8[cc][1] = lds8(c.sc + (c.rbase + c.g + 8) * c.SB + grp);
   }
+  float accs[NACC][NT][4];
+  zero_accs<NT, NACC>(accs);
+#pragma unroll
+  for (int cc = 0; cc < NCHK; ++cc) {
+    const uint32_t s2lo = prmt(e4m3x2_to_f16x2(sc8[cc][0]), 0u, 0x1010u);
+    const uint32_t s2hi = prmt(e4m3x2_to_f16x2(sc8[cc][1]), 0u, 0x1010u);
+    const uint32_t wlo = r[cc >> 1][2 * (cc & 1)], whi = r[cc >> 1][2 * (cc & 1) + 1];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t A[4] = {hmul2(e2m1x2_to_f16x2(wlo >> (16 * h)), s2lo),
+                             hmul2(e2m1x2_to_f16x2(whi >> (16 * h)), s2hi),
+                             hmul2(e2m1x2_to_f16x2(wlo >> (16 * h + 8)), s2lo),
+                             hmul2(e2m1x2_to_f16x2(whi >> (16 * h + 8)), s2hi)};
+      mma_f16_acc<NT>(accs[(2 * cc + h) % NACC], A, b0[2 * cc + h], b1[2 * cc + h], false);
+    }
+  }
+  fold_accs<NT, NACC>(acc, accs);
 }
 
 // BF16: a chunk pair is one standard 16-k step
-template <int NT, int CPB, int NB>
-FP4X_DEV void stage_bf16(const WarpCtx& c, float (&acc)[NT][4]) {
-  constexpr int SPB = CPB / 2, NS_ = NB * SPB, NACC = 2;
+template <int NT, int NCHK>
+FP4X_DEV void stage_bf16(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) {
+  constexpr int NS_ = NCHK / 2, NACC = NS_ < 2 ? 1 : 2;
+  const int S0 = (b * c.CPB + c0) >> 1;
   uint32_t A[NS_][4];
   uint32_t b0[NS_][NT], b1[NS_][NT];
 #pragma unroll
-  for (int s = 0; s < NS_; ++s) ld_pair(c, s / SPB, 2 * (s % SPB), A[s][0], A[s][1], A[s][2], A[s][3]);
+  for (int s = 0; s < NS_; ++s) ld_pair(c, b, c0 + 2 * s, A[s][0], A[s][1], A[s][2], A[s][3]);
 #pragma unroll
-  for (int s = 0; s < NS_; ++s) load_b<NT>(c, s, b0[s], b1[s]);
+  for (int s = 0; s < NS_; ++s) load_b<NT>(c, S0 + s, b0[s], b1[s]);
   float accs[NACC][NT][4];
   zero_accs<NT, NACC>(accs);
 #pragma unroll
@@ -591,73 +595,76 @@ FP4X_DEV void int2_table(uint32_t s16, uint32_t& tlo, uint32_t& thi) {
 
 // INT2: a chunk C is 64 k = four 16-groups; thread tq owns group 4C + tq; steps 4C + p.
 // Processed in 128-k units (two chunks, eight steps) to bound the registers held.  The four partial sums are folded
-// into `acc` after every unit, so a row's summation order depends on K alone and not on the stage shape the planner
-// picked: vocabulary shards of one head then give bit-identical logits.
-template <int NT, int CPB, int NB>
-FP4X_DEV void stage_int2(const WarpCtx& c, float (&acc)[NT][4]) {
+// into `acc` after every unit, so a row's summation order within a k-group's chunks depends on K alone and not on
+// the grid: vocabulary shards of one head then give bit-identical logits.
+template <int NT, int NCHK>
+FP4X_DEV void stage_int2(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) {
   constexpr int NACC = 4;
 #pragma unroll
-  for (int b = 0; b < NB; ++b) {
+  for (int u = 0; u < NCHK / 2; ++u) {
+    float accs[NACC][NT][4];
+    zero_accs<NT, NACC>(accs);
+    uint32_t rr[4];
+    ld_pair(c, b, c0 + 2 * u, rr[0], rr[1], rr[2], rr[3]);
+    const int C0 = b * c.CPB + c0 + 2 * u;
+    uint32_t s16[2][2];
 #pragma unroll
-    for (int u = 0; u < CPB / 2; ++u) {
-      float accs[NACC][NT][4];
-      zero_accs<NT, NACC>(accs);
-      uint32_t rr[4];
-      ld_pair(c, b, 2 * u, rr[0], rr[1], rr[2], rr[3]);
-      const int C0 = b * CPB + 2 * u;
-      uint32_t s16[2][2];
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        const int sidx = (4 * (C0 + cc) + c.tq) >> c.gshift;
-        s16[cc][0] = lds16(c.sc + (c.rbase + c.g) * c.SB + 2 * sidx);
-        s16[cc][1] = lds16(c.sc + (c.rbase + c.g + 8) * c.SB + 2 * sidx);
-      }
-      uint32_t b0[8][NT], b1[8][NT];
-#pragma unroll
-      for (int s = 0; s < 8; ++s) load_b<NT>(c, 4 * C0 + s, b0[s], b1[s]);
-#pragma unroll
-      for (int cc = 0; cc < 2; ++cc) {
-        uint32_t tlo[2], thi[2];
-        int2_table(s16[cc][0], tlo[0], thi[0]);
-        int2_table(s16[cc][1], tlo[1], thi[1]);
-        const uint32_t W[2] = {rr[2 * cc], rr[2 * cc + 1]};
-#pragma unroll
-        for (int p = 0; p < 4; ++p) {
-          uint32_t A[4];
-#pragma unroll
-          for (int q = 0; q < 2; ++q) {
-            const uint32_t z = (W[q] >> (2 * p)) & 0x03030303u;
-            const uint32_t sl = z * 0x11u + 0x4040u;
-            const uint32_t sh = __umulhi(z, 0x110000u) + 0x4040u;
-            A[q] = prmt(tlo[q], thi[q], sl);
-            A[2 + q] = prmt(tlo[q], thi[q], sh);
-          }
-          mma_bf16_acc<NT>(accs[p], A, b0[4 * cc + p], b1[4 * cc + p]);
-        }
-      }
-      fold_accs<NT, NACC>(acc, accs);
+    for (int cc = 0; cc < 2; ++cc) {
+      const int sidx = (4 * (C0 + cc) + c.tq) >> c.gshift;
+      s16[cc][0] = lds16(c.sc + (c.rbase + c.g) * c.SB + 2 * sidx);
+      s16[cc][1] = lds16(c.sc + (c.rbase + c.g + 8) * c.SB + 2 * sidx);
     }
+    uint32_t b0[8][NT], b1[8][NT];
+#pragma unroll
+    for (int s = 0; s < 8; ++s) load_b<NT>(c, 4 * C0 + s, b0[s], b1[s]);
+#pragma unroll
+    for (int cc = 0; cc < 2; ++cc) {
+      uint32_t tlo[2], thi[2];
+      int2_table(s16[cc][0], tlo[0], thi[0]);
+      int2_table(s16[cc][1], tlo[1], thi[1]);
+      const uint32_t W[2] = {rr[2 * cc], rr[2 * cc + 1]};
+#pragma unroll
+      for (int p = 0; p < 4; ++p) {
+        uint32_t A[4];
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const uint32_t z = (W[q] >> (2 * p)) & 0x03030303u;
+          const uint32_t sl = z * 0x11u + 0x4040u;
+          const uint32_t sh = __umulhi(z, 0x110000u) + 0x4040u;
+          A[q] = prmt(tlo[q], thi[q], sl);
+          A[2 + q] = prmt(tlo[q], thi[q], sh);
+        }
+        mma_bf16_acc<NT>(accs[p], A, b0[4 * cc + p], b1[4 * cc + p]);
+      }
+    }
+    fold_accs<NT, NACC>(acc, accs);
   }
 }
 
-template <int FMT, int NT, int CPB, int NB>
-FP4X_DEV void stage_shape(const WarpCtx& c, float (&acc)[NT][4]) {
-  if (FMT == FMT_MX8) stage_mx8<NT, CPB, NB>(c, acc);
-  else if (FMT == FMT_W8) stage_w8<NT, CPB, NB>(c, acc);
-  else if (FMT == FMT_W6) stage_w6<NT, CPB, NB>(c, acc);
-  else if (FMT == FMT_NV4) stage_nv4<NT, CPB, NB>(c, acc);
-  else if (FMT == FMT_BF16) stage_bf16<NT, CPB, NB>(c, acc);
-  else stage_int2<NT, CPB, NB>(c, acc);
+template <int FMT, int NT, int NCHK>
+FP4X_DEV void stage_range(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) {
+  if constexpr (FMT == FMT_MX8) stage_mx8<NT, NCHK>(c, b, c0, acc);
+  else if constexpr (FMT == FMT_W8) stage_w8<NT, NCHK>(c, b, c0, acc);
+  else if constexpr (FMT == FMT_W6) stage_w6<NT, NCHK>(c, b, c0, acc);
+  else if constexpr (FMT == FMT_NV4) stage_nv4<NT, NCHK>(c, b, c0, acc);
+  else if constexpr (FMT == FMT_BF16) stage_bf16<NT, NCHK>(c, b, c0, acc);
+  else stage_int2<NT, NCHK>(c, b, c0, acc);
 }
 
-// stage shapes used by the planner: (128-byte boxes, 2 per stage), (128, 1), (64, 1)
+// This k-group's half of a stage.  Stage shapes used by the planner: two 128-byte boxes (each k-group takes one
+// box), one 128-byte box (four chunks each), one 64-byte box (two chunks each; a W8 64-group spans the whole box, so
+// k-group 0 takes it alone).
 template <int FMT, int NT>
-FP4X_DEV void compute_stage(const WarpCtx& c, float (&acc)[NT][4]) {
+FP4X_DEV void compute_stage(const WarpCtx& c, int kg, float (&acc)[NT][4]) {
   if (c.BI0 == 128) {
-    if (c.NB0 == 2) stage_shape<FMT, NT, 8, 2>(c, acc);
-    else stage_shape<FMT, NT, 8, 1>(c, acc);
+    if (c.NB0 == 2) stage_range<FMT, NT, 8>(c, kg, 0, acc);
+    else stage_range<FMT, NT, 4>(c, 0, 4 * kg, acc);
   } else {
-    stage_shape<FMT, NT, 4, 1>(c, acc);
+    if constexpr (FMT == FMT_W8) {
+      if (kg == 0) stage_range<FMT, NT, 4>(c, 0, 0, acc);
+    } else {
+      stage_range<FMT, NT, 2>(c, 0, 2 * kg, acc);
+    }
   }
 }
 
@@ -759,7 +766,7 @@ FP4X_DEV void run_epilogue(const GemvArgs& A, const GemvItem& it, int row0, cons
 // the kernel
 // ------------------------------------------------------------------------------------------------------
 template <int FMT, int NT, int EPI>
-__global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ GemvArgs A) {
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvArgs A) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   // stages need 1024-byte alignment for the swizzled TMA tiles; the host adds 1 KB of slack
   uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -780,6 +787,8 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + A.smem_misc + 128);
   const uint32_t full0 = smem_u32(bars), empty0 = smem_u32(bars + kMaxStages);
   const uint32_t xbar = smem_u32(bars + 2 * kMaxStages);
+  // k-group handshake per row warp: comb_full (k-group 1 has left its sums), comb_empty (k-group 0 has read them)
+  const uint32_t comb_full0 = smem_u32(bars + 2 * kMaxStages + 1), comb_empty0 = comb_full0 + 8 * kRW;
   const int CPP = A.CPP;
   const int cta = blockIdx.x;
   const int64_t Up = A.whole ? (int64_t)A.RT : (int64_t)A.RT * A.NCH;
@@ -793,6 +802,10 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
       mbar_init(empty0 + 8 * s, kCWarps);
     }
     mbar_init(xbar, 1);
+    for (int i = 0; i < kRW; ++i) {
+      mbar_init(comb_full0 + 8 * i, 1);
+      mbar_init(comb_empty0 + 8 * i, 1);
+    }
     mbar_init_fence();
   }
   __syncthreads();
@@ -843,6 +856,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
 
   // ---------------- consumer warps ----------------
   const int g = lane >> 2, tq = lane & 3;
+  const int wrow = warp & (kRW - 1), kg = warp / kRW;
   pdl_wait();
   stage_activations<FMT>(A, it, base, MP, k_panel0, xbar);
   named_bar(1, kCWarps * 32);
@@ -851,11 +865,11 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
   const float* xsc = reinterpret_cast<const float*>(base + A.smem_misc);
   float* scr = reinterpret_cast<float*>(base + A.smem_scr);
   WarpCtx wc;
-  wc.BI0 = A.BI0; wc.BI1 = A.BI1; wc.NB0 = A.NB0; wc.SB = A.SB; wc.XP = A.XP;
-  wc.g = g; wc.tq = tq; wc.rbase = 16 * warp;
+  wc.BI0 = A.BI0; wc.BI1 = A.BI1; wc.NB0 = A.NB0; wc.SB = A.SB; wc.XP = A.XP; wc.CPB = A.BI0 / 16;
+  wc.g = g; wc.tq = tq; wc.rbase = 16 * wrow;
   wc.gshift = A.group == 32 ? 1 : 0;
   {
-    const int r = 16 * warp + (lane & 7) + 8 * ((lane >> 3) & 1);
+    const int r = 16 * wrow + (lane & 7) + 8 * ((lane >> 3) & 1);
     wc.lrow0 = (uint32_t)(r * A.BI0);
     wc.lswz = A.BI0 == 128 ? (r & 7) : ((r >> 1) & 3);
     wc.lsel = lane >> 4;
@@ -867,15 +881,39 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
   zero4<NT>(acc);
   int cur = -1;
   bool ok = true;
+  uint32_t nflush = 0;
+  float* comb = reinterpret_cast<float*>(base + A.smem_comb) + (wrow * 32 + lane) * (NT * 4);
 
   auto flush = [&](int blk) {
+    // k-group 1 hands its partial sums for these 16 rows to k-group 0 through shared memory
+    const uint32_t cf_bar = comb_full0 + 8 * wrow, ce_bar = comb_empty0 + 8 * wrow;
+    const uint32_t par = nflush & 1u;
+    ++nflush;
+    if (kg == 1) {
+      // the previous block's sums must have been read before this block's overwrite them
+      if (nflush > 1 && !mbar_wait_bounded(ce_bar, par ^ 1u, A.err)) { ok = false; return; }
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+        *reinterpret_cast<float4*>(comb + 4 * t) = make_float4(acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(cf_bar);
+      return;
+    }
+    if (!mbar_wait_bounded(cf_bar, par, A.err)) { ok = false; return; }
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const float4 o = *reinterpret_cast<const float4*>(comb + 4 * t);
+      acc[t][0] += o.x; acc[t][1] += o.y; acc[t][2] += o.z; acc[t][3] += o.w;
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(ce_bar);
     if (G.xf16) {
 #pragma unroll
       for (int t = 0; t < NT; ++t)
 #pragma unroll
         for (int e = 0; e < 4; ++e) acc[t][e] *= xsc[MP + 8 * t + 2 * tq + (e & 1)];
     }
-    const int row0 = blk * kRB + 16 * warp;
+    const int row0 = blk * kRB + 16 * wrow;
     int cf, cl;
     if (A.whole) {
       cf = cl = cta;
@@ -886,7 +924,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
     }
     const int segs = cl - cf + 1;
     if (A.KP == 1 && segs == 1) {
-      run_epilogue<EPI, NT>(A, it, row0, acc, warp, g, tq, scr);
+      run_epilogue<EPI, NT>(A, it, row0, acc, wrow, g, tq, scr);
       return;
     }
     auto slot_of = [&](int pp, int cc) -> int64_t {
@@ -897,7 +935,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
       } else {
         s = (((int64_t)b * A.KP + pp) * A.RT + blk) * A.SMAX + (cc - cf);
       }
-      return s * kCWarps + warp;
+      return s * kRW + wrow;
     };
     float* mine = A.ws + slot_of(p, cta) * (16 * MP);
 #pragma unroll
@@ -909,7 +947,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
     // The warp barrier orders every lane's partial stores before lane 0's release; the acquire half of the same
     // atomic, followed by the warp barrier, orders the last arriver's reads of the other partials after it.
     __syncwarp();
-    int* semp = A.sem + ((int64_t)b * A.RT + blk) * kCWarps + warp;
+    int* semp = A.sem + ((int64_t)b * A.RT + blk) * kRW + wrow;
     int last = 0;
     if (lane == 0) last = (atomic_add_acq_rel(semp, 1) == A.KP * segs - 1);
     last = __shfl_sync(0xffffffffu, last, 0);
@@ -928,7 +966,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
           tot[t][0] += lo.x; tot[t][1] += lo.y; tot[t][2] += hi.x; tot[t][3] += hi.y;
         }
       }
-    run_epilogue<EPI, NT>(A, it, row0, tot, warp, g, tq, scr);
+    run_epilogue<EPI, NT>(A, it, row0, tot, wrow, g, tq, scr);
     if (lane == 0) atomicExch(semp, 0);
   };
 
@@ -947,7 +985,7 @@ __global__ void __launch_bounds__(kThreads) gemv_kernel(const __grid_constant__ 
     wc.p1 = stage + A.off_p1;
     wc.sc = stage + A.off_sc;
     wc.xb = xrow + chunk * steps_per_stage * 32;
-    compute_stage<FMT, NT>(wc, acc);
+    compute_stage<FMT, NT>(wc, kg, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * s);
     if (++s == A.NS) { s = 0; phase ^= 1u; }
