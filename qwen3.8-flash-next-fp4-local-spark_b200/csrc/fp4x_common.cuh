@@ -74,6 +74,54 @@ FP4X_DEV bool mbar_wait_bounded(uint32_t bar, uint32_t parity, int* err, uint64_
   }
 }
 
+// ---- thread-block clusters (distributed shared memory) ----
+FP4X_DEV uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// all threads of all CTAs of the cluster (the CTAs of a cluster are co-scheduled, so every CTA reaches it)
+FP4X_DEV void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// the shared::cluster address of `addr` (a shared::cta address of this CTA) in the CTA of rank `rank`
+FP4X_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
+  return r;
+}
+FP4X_DEV void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
+  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+               : "memory");
+}
+// arrive on an mbarrier of another CTA of the cluster, releasing this thread's prior writes at cluster scope
+FP4X_DEV void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+FP4X_DEV bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// bounded wait whose completion acquires writes released at cluster scope by other CTAs
+FP4X_DEV bool mbar_wait_bounded_cluster(uint32_t bar, uint32_t parity, int* err, uint64_t limit_ns = 2000000000ull) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const uint64_t t0 = global_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 255u) == 0 && global_ns() - t0 > limit_ns) {
+      set_dev_error(err, kDevWaitTimeout);
+      return false;
+    }
+  }
+}
+
 // one contiguous global -> shared copy handled by the bulk-copy engine; completes on `bar` (tx bytes)
 FP4X_DEV void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
   asm volatile(

@@ -78,6 +78,22 @@ cudaError_t ensure_smem_attr(const void* kernel, int bytes) {
   return e;
 }
 
+// allow clusters of up to 16 CTAs for a kernel, once per (kernel, device)
+static cudaError_t ensure_nonportable_cluster(const void* kernel) {
+  static const void* done_k[256];
+  static int done_d[256];
+  static int n = 0;
+  static std::mutex mu;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lk(mu);
+  for (int i = 0; i < n; ++i)
+    if (done_k[i] == kernel && done_d[i] == dev) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+  if (e == cudaSuccess && n < 256) { done_k[n] = kernel; done_d[n] = dev; ++n; }
+  return e;
+}
+
 // ------------------------------------------------------------------------------------------------------
 // TMA descriptors: 2D [rows, row_bytes] uint8 views, box {inner, 64 rows}, 64B/128B swizzle; cached per device
 // ------------------------------------------------------------------------------------------------------
@@ -154,7 +170,8 @@ struct Plan {
   int NT, MP;
   int KPW, KP, KC, NCH, CPP, RT, NS, SMAX, whole;
   int BI0, BI1, NB0, SB, STG, off_p1, off_sc, XP;
-  int smem_x, smem_misc, smem_scr, smem_xraw, smem_comb, smem_total;
+  int smem_x, smem_misc, smem_scr, smem_xraw, smem_comb, smem_red, smem_total;
+  int cluster;
   size_t ws_bytes;
   int64_t counters;
 };
@@ -180,6 +197,59 @@ static bool chunk_for(int fmt, int kpw, int& KC, int& BI0, int& NB0) {
     KC = kc;
     BI0 = pb >= 128 ? 128 : 64;
     NB0 = pb / BI0;
+    return true;
+  }
+  return false;
+}
+
+// Cluster plan: one row block per CTA, K split into KP panels (2..8) whose CTAs form a (1, KP, 1) cluster; the
+// panel partials are summed in the leader's shared memory.  Picks the largest KP with RT * KP <= 2 * SMs whose panel
+// width has a valid stage shape.  `base` carries the shape fields (NT, MP, RT).
+static bool make_cluster_plan(int fmt, int64_t M, int64_t N, int64_t K, int group, const Plan& base, Plan& out) {
+  const FmtGeom G = fmt_geom(fmt);
+  const DeviceFacts& dv = device_facts();
+  const int sd = fmt == FMT_INT2 ? group / 2 : G.sd;
+  const int misc = 512;
+  const int comb_bytes = kRW * 32 * base.NT * 4 * 4;
+  for (int KP = 8; KP >= 2; --KP) {
+    if (K % KP || (int64_t)base.RT * KP > 2 * dv.sms) continue;
+    const int kpw = (int)(K / KP);
+    int KC, BI0, NB0;
+    if (kpw % 64 || !chunk_for(fmt, kpw, KC, BI0, NB0)) continue;
+    if (fmt == FMT_W8 && BI0 == 64) continue;  // one 64-group per stage would leave a k-group idle
+    Plan c = base;
+    c.KPW = kpw; c.KP = KP; c.KC = KC; c.BI0 = BI0; c.NB0 = NB0; c.NCH = kpw / KC;
+    c.BI1 = G.n1 ? KC * G.n1 / G.d1 : 0;
+    c.SB = G.sn ? KC * G.sn / sd : 0;
+    if (c.SB % 4) continue;
+    c.off_p1 = kRB * NB0 * BI0;
+    c.off_sc = c.off_p1 + kRB * c.BI1;
+    c.STG = round_up(c.off_sc + kRB * c.SB, 1024);
+    c.XP = (kpw / 16) * 32 + 32;
+    const int red_bytes = (KP - 1) * kRW * 32 * c.NT * 16;
+    const int xbytes = round_up(c.MP * c.XP, 16) + (int)M * kpw * 2;
+    const int fixed = xbytes + misc + comb_bytes + red_bytes + 1024;
+    const int ctas = base.RT * KP;
+    const int cap = ctas > dv.sms ? dv.smem_sm / 2 - 2048 : dv.smem_optin;
+    int ns = (cap - fixed) / c.STG;
+    if (ns > kMaxStages) ns = kMaxStages;
+    if (ns > c.NCH) ns = c.NCH;  // a CTA streams NCH stages in all
+    if (ns < 1 || (c.NCH > 1 && ns < 2)) continue;
+    c.NS = ns;
+    c.CPP = base.RT;
+    c.whole = 1;
+    c.SMAX = 1;
+    c.smem_x = c.NS * c.STG;
+    c.smem_misc = c.smem_x + round_up(c.MP * c.XP, 16);
+    c.smem_scr = c.smem_misc + misc;
+    c.smem_xraw = c.smem_scr;
+    c.smem_comb = c.smem_xraw + round_up((int)M * kpw * 2, 16);
+    c.smem_red = c.smem_comb + comb_bytes;
+    c.smem_total = c.smem_red + red_bytes + 1024;
+    c.ws_bytes = 0;
+    c.counters = 0;
+    c.cluster = KP;
+    out = c;
     return true;
   }
   return false;
@@ -284,6 +354,13 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
   else
     pl.ws_bytes = 0;
   pl.counters = (pl.KP > 1 || split) ? (int64_t)batch * pl.RT * kRW : 0;
+  pl.cluster = 0;
+  pl.smem_red = pl.smem_total;
+  // Small row counts: split K into panels whose CTAs form one cluster per row block and reduce on chip.
+  if (mode == kStreamK && !whole && batch == 1 && fmt != FMT_INT2 && 2 * pl.RT <= dv.sms) {
+    Plan cp;
+    if (make_cluster_plan(fmt, M, N, K, group, pl, cp)) pl = cp;
+  }
   return FP4X_OK;
 }
 
@@ -295,6 +372,15 @@ static int launch_t(const Plan& pl, const GemvArgs& a, int64_t batch, cudaStream
   auto kern = gemv_kernel<FMT, NT, EPI>;
   cudaError_t e = ensure_smem_attr((const void*)kern, pl.smem_total);
   if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
+  if (pl.cluster > 1) {
+    if (pl.cluster > 8) {
+      e = ensure_nonportable_cluster((const void*)kern);
+      if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute(non-portable cluster)");
+    }
+    return check_launch(launch_pdl_cluster(kern, dim3(pl.CPP, pl.KP, (unsigned)batch), dim3(kThreads), pl.smem_total,
+                                           st, pl.cluster, a),
+                        "gemv cluster launch");
+  }
   return check_launch(launch_pdl(kern, dim3(pl.CPP, pl.KP, (unsigned)batch), dim3(kThreads), pl.smem_total, st, a),
                       "gemv launch");
 }
@@ -312,6 +398,7 @@ static void fill_args(const Plan& pl, GemvArgs& a) {
   a.off_p1 = pl.off_p1; a.off_sc = pl.off_sc; a.XP = pl.XP;
   a.smem_x = pl.smem_x; a.smem_misc = pl.smem_misc; a.smem_scr = pl.smem_scr; a.smem_xraw = pl.smem_xraw;
   a.smem_comb = pl.smem_comb;
+  a.cluster = pl.cluster; a.smem_red = pl.smem_red;
 }
 
 // widest cp.async (16/8/4 bytes) that keeps every scale copy aligned

@@ -102,6 +102,8 @@ struct alignas(64) GemvArgs {
   int smem_x, smem_misc, smem_scr;  // offsets of the regions after the 1024-aligned base (stages start at 0)
   int smem_xraw;          // raw bf16 activation panel [M][KPW] (bulk-copied after griddepcontrol.wait)
   int smem_comb;          // k-group hand-over of partial sums: [kRW][32 lanes][NT * 4] fp32
+  int cluster;            // > 1: the KP panel CTAs of a row block form a cluster and reduce through its leader
+  int smem_red;           // cluster leader: partial sums of the other panels [cluster - 1][kRW][32][NT * 4] fp32
   int lr, hc, bj;         // hyper-connection epilogues
   const void* nrm;        // HC up: normalized input [M, hc*H]
   int64_t nrm_stride;
@@ -789,6 +791,8 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
   const uint32_t xbar = smem_u32(bars + 2 * kMaxStages);
   // k-group handshake per row warp: comb_full (k-group 1 has left its sums), comb_empty (k-group 0 has read them)
   const uint32_t comb_full0 = smem_u32(bars + 2 * kMaxStages + 1), comb_empty0 = comb_full0 + 8 * kRW;
+  // cluster leader: one barrier per row warp that the other panels' CTAs arrive on remotely
+  const uint32_t red_full0 = comb_empty0 + 8 * kRW;
   const int CPP = A.CPP;
   const int cta = blockIdx.x;
   const int64_t Up = A.whole ? (int64_t)A.RT : (int64_t)A.RT * A.NCH;
@@ -805,10 +809,13 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     for (int i = 0; i < kRW; ++i) {
       mbar_init(comb_full0 + 8 * i, 1);
       mbar_init(comb_empty0 + 8 * i, 1);
+      if (A.cluster > 1) mbar_init(red_full0 + 8 * i, A.cluster - 1);
     }
     mbar_init_fence();
   }
   __syncthreads();
+  // the leader's barriers must be initialised before another CTA of the cluster arrives on them
+  if (A.cluster > 1) cluster_sync_all();
 
   if (warp == kCWarps) {
     // ---------------- producer warp ----------------
@@ -914,6 +921,38 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
         for (int e = 0; e < 4; ++e) acc[t][e] *= xsc[MP + 8 * t + 2 * tq + (e & 1)];
     }
     const int row0 = blk * kRB + 16 * wrow;
+    if (A.cluster > 1) {
+      // One row block per CTA; the CTAs of the block's K panels form the cluster.  Each non-leader writes its
+      // partial sums into the leader's shared memory and arrives on the leader's barrier for this row warp; the
+      // leader adds them in panel order and runs the epilogue.
+      const uint32_t rank = cluster_ctarank();
+      constexpr uint32_t kSlot = 32u * NT * 16u;  // one row warp: 32 lanes x NT float4
+      const uint32_t red = smem_u32(base + A.smem_red) + (uint32_t)wrow * kSlot + (uint32_t)lane * NT * 16u;
+      if (rank != 0) {
+        const uint32_t dst = mapa_shared(red + (rank - 1) * kRW * kSlot, 0);
+#pragma unroll
+        for (int t = 0; t < NT; ++t) st_cluster_v4(dst + 16u * t, acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote(mapa_shared(red_full0 + 8 * wrow, 0));
+        return;
+      }
+      if (!mbar_wait_bounded_cluster(red_full0 + 8 * wrow, 0, A.err)) { ok = false; return; }
+      float tot[NT][4];
+#pragma unroll
+      for (int t = 0; t < NT; ++t)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) tot[t][e] = acc[t][e];
+      for (int r = 1; r < A.cluster; ++r) {
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          const float4 v = *reinterpret_cast<const float4*>(base + A.smem_red + (r - 1) * kRW * kSlot +
+                                                            wrow * kSlot + lane * NT * 16 + 16 * t);
+          tot[t][0] += v.x; tot[t][1] += v.y; tot[t][2] += v.z; tot[t][3] += v.w;
+        }
+      }
+      run_epilogue<EPI, NT>(A, it, row0, tot, wrow, g, tq, scr);
+      return;
+    }
     int cf, cl;
     if (A.whole) {
       cf = cl = cta;
@@ -953,19 +992,39 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     last = __shfl_sync(0xffffffffu, last, 0);
     __syncwarp();
     if (!last) return;
+    // Sum the partial slots in the fixed order (panel, then CTA).  The loads of eight slots are issued before any
+    // of them is added (four at M > 8), so their L2 latencies overlap instead of adding up.
     float tot[NT][4];
     zero4<NT>(tot);
-    for (int pp = 0; pp < A.KP; ++pp)
-      for (int cc = cf; cc <= cl; ++cc) {
-        const float* src = A.ws + slot_of(pp, cc) * (16 * MP);
+    const int nslots = A.KP * segs;
+    constexpr int kBatch = 8 / NT;
+    for (int i0 = 0; i0 < nslots; i0 += kBatch) {
+      float2 v[kBatch][NT][2];
 #pragma unroll
-        for (int t = 0; t < NT; ++t) {
-          const int m = 8 * t + 2 * tq;
-          const float2 lo = __ldcg(reinterpret_cast<const float2*>(src + g * MP + m));
-          const float2 hi = __ldcg(reinterpret_cast<const float2*>(src + (g + 8) * MP + m));
-          tot[t][0] += lo.x; tot[t][1] += lo.y; tot[t][2] += hi.x; tot[t][3] += hi.y;
+      for (int j = 0; j < kBatch; ++j) {
+        const int i = i0 + j;
+        if (i < nslots) {
+          const int pp = i / segs, cc = cf + (i - pp * segs);
+          const float* src = A.ws + slot_of(pp, cc) * (16 * MP);
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            const int m = 8 * t + 2 * tq;
+            v[j][t][0] = __ldcg(reinterpret_cast<const float2*>(src + g * MP + m));
+            v[j][t][1] = __ldcg(reinterpret_cast<const float2*>(src + (g + 8) * MP + m));
+          }
         }
       }
+#pragma unroll
+      for (int j = 0; j < kBatch; ++j) {
+        if (i0 + j < nslots) {
+#pragma unroll
+          for (int t = 0; t < NT; ++t) {
+            tot[t][0] += v[j][t][0].x; tot[t][1] += v[j][t][0].y;
+            tot[t][2] += v[j][t][1].x; tot[t][3] += v[j][t][1].y;
+          }
+        }
+      }
+    }
     run_epilogue<EPI, NT>(A, it, row0, tot, wrow, g, tq, scr);
     if (lane == 0) atomicExch(semp, 0);
   };

@@ -42,6 +42,29 @@ cudaError_t launch_pdl(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaSt
   return e;
 }
 
+// the same with a thread-block cluster of (1, cluster_y, 1) CTAs
+template <typename Kernel, typename... Args>
+cudaError_t launch_pdl_cluster(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream, int cluster_y,
+                               Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = (unsigned)cluster_y;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (e == cudaSuccess) g_launches.fetch_add(1, std::memory_order_relaxed);
+  return e;
+}
+
 // address of the device error word on the current device (cudaGetSymbolAddress, cached per device)
 int* dev_error_ptr();
 
