@@ -367,9 +367,9 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
 // ------------------------------------------------------------------------------------------------------
 // launch
 // ------------------------------------------------------------------------------------------------------
-template <int FMT, int NT, int EPI>
-static int launch_t(const Plan& pl, const GemvArgs& a, int64_t batch, cudaStream_t st) {
-  auto kern = gemv_kernel<FMT, NT, EPI>;
+template <int FMT, int NT, int EPI, int SHAPE>
+static int launch_s(const Plan& pl, const GemvArgs& a, int64_t batch, cudaStream_t st) {
+  auto kern = gemv_kernel<FMT, NT, EPI, SHAPE>;
   cudaError_t e = ensure_smem_attr((const void*)kern, pl.smem_total);
   if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
   if (pl.cluster > 1) {
@@ -383,6 +383,15 @@ static int launch_t(const Plan& pl, const GemvArgs& a, int64_t batch, cudaStream
   }
   return check_launch(launch_pdl(kern, dim3(pl.CPP, pl.KP, (unsigned)batch), dim3(kThreads), pl.smem_total, st, a),
                       "gemv launch");
+}
+
+template <int FMT, int NT, int EPI>
+static int launch_t(const Plan& pl, const GemvArgs& a, int64_t batch, cudaStream_t st) {
+  if (pl.BI0 == 128) {
+    if (pl.NB0 == 2) return launch_s<FMT, NT, EPI, SHAPE_128x2>(pl, a, batch, st);
+    return launch_s<FMT, NT, EPI, SHAPE_128x1>(pl, a, batch, st);
+  }
+  return launch_s<FMT, NT, EPI, SHAPE_64x1>(pl, a, batch, st);
 }
 
 template <int FMT, int EPI>

@@ -656,17 +656,20 @@ FP4X_DEV void stage_range(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) 
 // This k-group's half of a stage.  Stage shapes used by the planner: two 128-byte boxes (each k-group takes one
 // box), one 128-byte box (four chunks each), one 64-byte box (two chunks each; a W8 64-group spans the whole box, so
 // k-group 0 takes it alone).
-template <int FMT, int NT>
+// The stage shape is a template parameter of the kernel (SHAPE_*), so each kernel holds the code of one shape:
+// the fully unrolled stage bodies are large, and a kernel carrying all three shapes runs out of instruction cache.
+enum StageShape : int { SHAPE_128x2 = 0, SHAPE_128x1 = 1, SHAPE_64x1 = 2 };
+
+template <int FMT, int NT, int SHAPE>
 FP4X_DEV void compute_stage(const WarpCtx& c, int kg, float (&acc)[NT][4]) {
-  if (c.BI0 == 128) {
-    if (c.NB0 == 2) stage_range<FMT, NT, 8>(c, kg, 0, acc);
-    else stage_range<FMT, NT, 4>(c, 0, 4 * kg, acc);
+  if constexpr (SHAPE == SHAPE_128x2) {
+    stage_range<FMT, NT, 8>(c, kg, 0, acc);
+  } else if constexpr (SHAPE == SHAPE_128x1) {
+    stage_range<FMT, NT, 4>(c, 0, 4 * kg, acc);
+  } else if constexpr (FMT == FMT_W8) {
+    if (kg == 0) stage_range<FMT, NT, 4>(c, 0, 0, acc);
   } else {
-    if constexpr (FMT == FMT_W8) {
-      if (kg == 0) stage_range<FMT, NT, 4>(c, 0, 0, acc);
-    } else {
-      stage_range<FMT, NT, 2>(c, 0, 2 * kg, acc);
-    }
+    stage_range<FMT, NT, 2>(c, 0, 2 * kg, acc);
   }
 }
 
@@ -767,7 +770,7 @@ FP4X_DEV void run_epilogue(const GemvArgs& A, const GemvItem& it, int row0, cons
 // ------------------------------------------------------------------------------------------------------
 // the kernel
 // ------------------------------------------------------------------------------------------------------
-template <int FMT, int NT, int EPI>
+template <int FMT, int NT, int EPI, int SHAPE>
 __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvArgs A) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   // stages need 1024-byte alignment for the swizzled TMA tiles; the host adds 1 KB of slack
@@ -1044,7 +1047,7 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     wc.p1 = stage + A.off_p1;
     wc.sc = stage + A.off_sc;
     wc.xb = xrow + chunk * steps_per_stage * 32;
-    compute_stage<FMT, NT>(wc, kg, acc);
+    compute_stage<FMT, NT, SHAPE>(wc, kg, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * s);
     if (++s == A.NS) { s = 0; phase ^= 1u; }
