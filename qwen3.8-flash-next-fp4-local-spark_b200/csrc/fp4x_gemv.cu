@@ -8,6 +8,7 @@
 #include <vector>
 
 #include "fp4x_gemv.cuh"
+#include "fp4x_tc.cuh"
 #include "fp4x_host.h"
 
 namespace fp4x {
@@ -445,6 +446,52 @@ static int check_rows(const void* p, int64_t row_bytes, const char* what) {
   return FP4X_OK;
 }
 
+// NVFP4 on tcgen05 block-scaled MMAs (fp4x_tc.cuh): M <= 8 tokens, at least 64 row blocks of 128, K a multiple
+// of 256.  Returns 1 when the shape is not covered (the caller then uses the register-decode kernel).
+static int run_nv4_tc(const void* x, int64_t x_stride, const void* wp, const void* sc, float gs, void* out,
+                      int64_t out_stride, int out_dtype, int64_t m, int64_t n, int64_t k, void* stream) {
+  const DeviceFacts& dv = device_facts();
+  if (m < 1 || m > tc::kMaxM || k % tc::kKC != 0 || n < 64 * tc::kRows || n > (1 << 30)) return 1;
+  const int NB = (tc::kTerms * (int)m + 15) / 16 * 16;
+  if (4 * (k / 64) > tc::kTmemCols - tc::kColSFB || NB > tc::kColSFA) return 1;
+  if (!aligned(x, 16) || x_stride % 8 != 0 || x_stride < k || !aligned(wp, 16) || (k / 2) % 16 != 0) return 1;
+  const int64_t lds = k / 16;
+  int scw = 0;
+  for (int w : {16, 8, 4})
+    if (lds % w == 0 && aligned(sc, w)) { scw = w; break; }
+  if (!scw || !out || out_stride < n) return 1;
+  int rc;
+  if ((rc = check_out_dtype(out_dtype))) return rc;
+  tc::Args a;
+  std::memset(&a, 0, sizeof(a));
+  const int b_bytes = (int)(k / 256) * NB * 128;
+  const int xraw = round_up((int)(m * k * 2), 1024);
+  const int sfb = round_up((int)(k / 64) * NB * 4, 1024);
+  const int fixed = b_bytes + xraw + sfb + 256 + 1024;
+  int ns = (dv.smem_optin - fixed) / tc::kStageBytes;
+  if (ns > tc::kMaxStages) ns = tc::kMaxStages;
+  if (ns > (int)(k / tc::kKC)) ns = (int)(k / tc::kKC);
+  if (ns < 2) return 1;
+  a.NS = ns;
+  a.smem_b = ns * tc::kStageBytes;          // multiple of 1024
+  a.smem_xraw = a.smem_b + b_bytes;
+  a.smem_sfb = a.smem_xraw + xraw;
+  a.smem_misc = a.smem_sfb + sfb;
+  const int smem_total = a.smem_misc + 256 + 1024;
+  if ((rc = encode_rows(&a.tm, wp, n, k / 2, 128))) return rc;
+  a.x = (const __nv_bfloat16*)x; a.x_stride = x_stride;
+  a.sc = (const uint8_t*)sc; a.lds = lds; a.scw = scw;
+  a.out = out; a.out_stride = out_stride; a.out_dtype = out_dtype; a.gs = gs;
+  a.M = (int)m; a.N = (int)n; a.K = (int)k; a.NB = NB;
+  a.err = dev_error_ptr();
+  cudaError_t e = ensure_smem_attr((const void*)tc::nv4_tc_kernel, smem_total);
+  if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
+  const unsigned grid = (unsigned)((n + tc::kRows - 1) / tc::kRows);
+  return check_launch(launch_pdl(tc::nv4_tc_kernel, dim3(grid), dim3(tc::kThreads), (size_t)smem_total,
+                                 (cudaStream_t)stream, a),
+                      "nv4 tcgen05 launch");
+}
+
 // shared path of the single-matrix GEMVs
 static int run_gemv(int fmt, const void* x, int64_t x_stride, const void* p0, const void* p1, const void* sc,
                     float post, int group, void* out, void* out2, int64_t out_stride, int out_dtype, int64_t m,
@@ -596,6 +643,8 @@ int fp4x_bf16_linear(const void* x, int64_t x_stride, const void* w, void* out, 
 int fp4x_nv4_linear(const void* x, int64_t x_stride, const void* wp, const void* s, float gs, void* out,
                     int64_t out_stride, int out_dtype, int64_t m, int64_t n, int64_t k, void* ws, size_t ws_bytes,
                     int32_t* counters, int64_t n_counters, void* stream) {
+  const int rc = run_nv4_tc(x, x_stride, wp, s, gs, out, out_stride, out_dtype, m, n, k, stream);
+  if (rc <= 0) return rc;
   return run_gemv(FMT_NV4, x, x_stride, wp, nullptr, s, gs, 16, out, nullptr, out_stride, out_dtype, m, n, k, ws,
                   ws_bytes, counters, n_counters, stream, EPI_STORE);
 }

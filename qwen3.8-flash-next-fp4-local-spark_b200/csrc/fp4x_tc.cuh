@@ -1,0 +1,393 @@
+// NVFP4 GEMV on the 5th-generation tensor cores (tcgen05, sm_100a).
+//
+// out[m, n] = gs * sum_k x[m, k] * (e2m1(W[n, k]) * e4m3(S[n, k / 16]))  -- the reference's _nv4 (x/fp4x_kernels.py:73-99)
+//
+// The weights are consumed as stored: TMA brings 128-row x 256-k tiles of packed e2m1 bytes into shared memory in
+// the 128-byte-swizzled K-major layout the MMA reads, and the e4m3 block scales go to tensor memory, where the
+// block-scaled MMA (kind::mxf4nvf4, block16) applies them.  No weight element passes through a register.
+//
+// The MMA needs its B operand in the same block-scaled e2m1 form, so each bf16 activation row is written as a short
+// sum of e2m1 terms, each with its own e4m3 scale per 16 elements (one B column per term and token):
+//   x' = x * 2^-e0 (e0: exponent of max |x| of the token, so |x'| < 2);  v_0 = x'
+//   for t = 0..T-1:  S_t = e4m3 scale >= max|v_t| / 6 over the 16-block, q_t = e2m1(v_t / S_t),
+//                    v_{t+1} = 4 (v_t - q_t S_t)
+//   x = 2^e0 * sum_t 4^-t q_t S_t + 2^e0 * 4^-T v_T
+// Each step shrinks the block's largest residual at least 16/3-fold and the factor 4 keeps the scales in e4m3's
+// range; after T = 6 terms the remainder is below 2^-13 of the token's largest element (the products themselves are
+// exact and accumulate in fp32).  The epilogue recombines the term columns with the factors 2^(e0 - 2t).
+//
+// Roles (256 threads): warp 0 streams weight tiles (TMA) and their scale bytes (cp.async); warp 1 owns the tensor
+// memory and one elected lane issues the MMAs; warps 4..7 (tensor-memory subpartitions 0..3) copy each stage's
+// scales into tensor memory and run the epilogue; warps 1..7 build the activation terms after the grid-dependency
+// wait.  Every wait is bounded; a failed wait records an error and the kernel still releases its tensor memory.
+#pragma once
+#include <cuda.h>
+
+#include "fp4x_common.cuh"
+
+namespace fp4x {
+namespace tc {
+
+constexpr int kThreads = 256;
+constexpr int kRows = 128;          // MMA M
+constexpr int kKC = 256;            // k per stage (128 bytes of e2m1 per row)
+constexpr int kMaxStages = 8;
+constexpr int kTerms = 6;
+constexpr int kMaxM = 8;            // tokens: kTerms * 8 = 48 B columns
+constexpr int kTmemCols = 512;
+// tensor-memory column plan: accumulator, A scales (16 columns per stage), B scales (4 columns per 64-k block: the
+// B-scale tile is laid out for 128 columns of B whatever the MMA's N, so each k-block's slot starts 4-aligned)
+constexpr int kColD = 0, kColSFA = 128, kColSFB = 256;
+constexpr int kStageA = kRows * 128;                    // 16 KB of packed weights per stage
+constexpr int kStageBytes = kStageA + kRows * 16;       // + 16 scale bytes per row
+
+struct Args {
+  CUtensorMap tm;             // weights [N rows][K/2 bytes] u8, box {128 bytes, 64 rows}, 128-byte swizzle
+  const __nv_bfloat16* x;
+  int64_t x_stride;
+  const uint8_t* sc;          // e4m3 block scales [N][K/16]
+  int64_t lds;
+  int scw;                    // scale copy width (16, 8 or 4 bytes)
+  void* out;
+  int64_t out_stride;
+  int out_dtype;
+  float gs;
+  int M, N, K;
+  int NB;                     // MMA N (B columns), kTerms * M rounded up to 16
+  int NS;                     // stages
+  int smem_b, smem_xraw, smem_sfb, smem_misc;
+  int* err;
+};
+
+// ---- tensor-core primitives ----
+FP4X_DEV uint64_t smem_desc_sw128(uint32_t addr) {
+  // K-major, 128-byte swizzle: 8-row atoms of 1024 bytes stacked along M/N (stride 1024), version 1 (sm_100)
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)1u << 16) | ((uint64_t)(1024u >> 4) << 32) |
+         ((uint64_t)1u << 46) | ((uint64_t)2u << 61);
+}
+FP4X_DEV uint32_t idesc_nvf4(int nb) {
+  // kind::mxf4nvf4: A, B e2m1 (1), K-major, N = nb, scales ue4m3, M = 128, K = 64
+  return (1u << 7) | (1u << 10) | ((uint32_t)(nb >> 3) << 17) | (8u << 24);
+}
+FP4X_DEV void mma_nvf4(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa, uint32_t sfb, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+FP4X_DEV void tc_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
+}
+FP4X_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+FP4X_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+FP4X_DEV void tc_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+FP4X_DEV void tc_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+FP4X_DEV void tc_st16(uint32_t taddr, const uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16};" ::"r"(taddr),
+      "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]), "r"(v[9]),
+      "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+      : "memory");
+}
+FP4X_DEV void tc_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15}, "
+      "[%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+        "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+
+// ---- conversions ----
+// (lo, hi) -> one byte of two e2m1 values (lo in the low nibble), round to nearest even, saturating at +-6
+FP4X_DEV uint32_t f32x2_to_e2m1x2(float lo, float hi) {
+  uint32_t d;
+  asm("{\n\t.reg .b8 t;\n\tcvt.rn.satfinite.e2m1x2.f32 t, %1, %2;\n\tcvt.u32.u8 %0, t;\n\t}" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+// the smallest e4m3 code whose value is >= v (v > 0, v <= 448)
+FP4X_DEV uint32_t e4m3_code_ceil(float v) {
+  uint16_t h;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(h) : "f"(0.0f), "f"(v));
+  uint32_t c = h & 0xffu;
+  if (e4m3_to_f32(c) < v) ++c;
+  return c;
+}
+
+// One 16-element block of token m: the kTerms e2m1 terms (8 bytes each) and their scale codes.
+FP4X_DEV void block_terms(float (&v)[16], uint32_t (&lo)[kTerms], uint32_t (&hi)[kTerms], uint32_t (&code)[kTerms]) {
+#pragma unroll
+  for (int t = 0; t < kTerms; ++t) {
+    float amax = 0.f;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    uint32_t c = 0;
+    float s = 0.f, inv = 0.f;
+    if (amax > 0.f) {
+      c = e4m3_code_ceil(amax * (1.0f / 6.0f));
+      s = e4m3_to_f32(c);
+      inv = 1.0f / s;
+    }
+    code[t] = c;
+    uint32_t b[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      b[i] = f32x2_to_e2m1x2(v[2 * i] * inv, v[2 * i + 1] * inv);
+      const uint32_t h = e2m1x2_to_f16x2(b[i]);
+      const float q0 = f16_bits_to_f32(h & 0xffffu), q1 = f16_bits_to_f32(h >> 16);
+      v[2 * i] = 4.0f * fmaf(-q0, s, v[2 * i]);
+      v[2 * i + 1] = 4.0f * fmaf(-q1, s, v[2 * i + 1]);
+    }
+    lo[t] = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
+    hi[t] = b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24);
+  }
+}
+
+// byte offset of (B column n, k) in the 128-byte-swizzled K-major B operand: slabs of 256 k, 8-column atoms
+FP4X_DEV uint32_t b_offset(int NB, int n, int k) {
+  const int slab = k >> 8, byte = (k & 255) >> 1;
+  const int r = n & 7, chunk = byte >> 4;
+  return (uint32_t)(slab * NB * 128 + (n >> 3) * 1024 + r * 128 + ((chunk ^ r) << 4) + (byte & 15));
+}
+
+__global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_constant__ Args A) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * kRows;
+  const int nstages = A.K / kKC;
+  const int nkb = A.K / 64;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + A.smem_misc);
+  const uint32_t full0 = smem_u32(bars), sfa0 = full0 + 8 * kMaxStages, empty0 = sfa0 + 8 * kMaxStages;
+  const uint32_t dfull = empty0 + 8 * kMaxStages, xbar = dfull + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + A.smem_misc + 8 * (3 * kMaxStages + 2));
+  uint32_t* amax_bits = tmem_slot + 1;          // [kMaxM] max |x| per token (float bits)
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(amax_bits + kMaxM);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < A.NS; ++s) {
+      mbar_init(full0 + 8 * s, 33);
+      mbar_init(sfa0 + 8 * s, 4);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    mbar_init(dfull, 1);
+    mbar_init(xbar, 1);
+    for (int m = 0; m < kMaxM; ++m) amax_bits[m] = 0u;
+    *abort_flag = 0;
+    mbar_init_fence();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---------------- producer: weight tiles and their scale bytes (static: no grid-dependency wait) -----------
+    pdl_launch_dependents();
+    const int words = 16 / A.scw;
+    for (int st = 0; st < nstages && ok; ++st) {
+      const int s = st % A.NS, round = st / A.NS;
+      if (round > 0 && !mbar_wait_bounded(empty0 + 8 * s, (uint32_t)((round - 1) & 1), A.err)) { ok = false; break; }
+      const uint32_t stage = smem_u32(base) + (uint32_t)s * kStageBytes;
+      const int k0 = st * kKC;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(full0 + 8 * s, (uint32_t)kStageA);
+        tma_load_2d(stage, &A.tm, k0 / 2, row0, full0 + 8 * s);
+        tma_load_2d(stage + kStageA / 2, &A.tm, k0 / 2, row0 + 64, full0 + 8 * s);
+      }
+      for (int w = lane; w < kRows * words; w += 32) {
+        const int r = w / words, cw = w - r * words;
+        const int row = min(row0 + r, A.N - 1);
+        const uint8_t* src = A.sc + (int64_t)row * A.lds + k0 / 16 + cw * A.scw;
+        const uint32_t dst = stage + kStageA + r * 16 + cw * A.scw;
+        if (A.scw == 16) cp_async16(dst, src);
+        else if (A.scw == 8) cp_async8(dst, src);
+        else cp_async4(dst, src);
+      }
+      cp_async_arrive_noinc(full0 + 8 * s);
+    }
+    asm volatile("cp.async.wait_all;" ::: "memory");
+  } else {
+    // ---------------- activations -> e2m1 terms (warps 1..7) ----------------
+    const int ptid = threadIdx.x - 32, pthreads = kThreads - 32;
+    pdl_wait();
+    const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(base + A.smem_xraw);
+    if (ptid == 0) {
+      const uint32_t bytes = (uint32_t)A.K * 2u;
+      mbar_arrive_expect_tx(xbar, bytes * (uint32_t)A.M);
+      for (int m = 0; m < A.M; ++m)
+        bulk_g2s(smem_u32(base + A.smem_xraw) + m * bytes, A.x + (int64_t)m * A.x_stride, bytes, xbar);
+    }
+    if (!mbar_wait_bounded(xbar, 0, A.err)) ok = false;
+    if (ok) {
+      for (int m = 0; m < A.M; ++m) {
+        uint32_t mx = 0;
+        for (int i = ptid; i < A.K / 8; i += pthreads) {
+          const uint4 q = reinterpret_cast<const uint4*>(xr + (int64_t)m * A.K)[i];
+          const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            mx = max(mx, (w4[e] << 17) >> 1);  // |lo| as fp32 bits
+            mx = max(mx, (w4[e] >> 16 & 0x7fffu) << 16);
+          }
+        }
+#pragma unroll
+        for (int o = 16; o; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+        if (lane == 0) atomicMax(amax_bits + m, mx);
+      }
+    }
+    named_bar(1, pthreads);
+    if (ok) {
+      const int nblk = A.K / 16;
+      uint8_t* bsm = base + A.smem_b;
+      uint8_t* sfb = base + A.smem_sfb;
+      for (int idx = ptid; idx < A.M * nblk; idx += pthreads) {
+        const int m = idx / nblk, j = idx - m * nblk;
+        const uint32_t mb = amax_bits[m];
+        // 2^-e0 with e0 the exponent of the token maximum (1 for an all-zero token)
+        const int e0 = mb ? (int)(mb >> 23) - 127 : 0;
+        const float pre = __uint_as_float((uint32_t)(127 - max(min(e0, 126), -126)) << 23);
+        float v[16];
+        const uint4 q0 = reinterpret_cast<const uint4*>(xr + (int64_t)m * A.K + 16 * j)[0];
+        const uint4 q1 = reinterpret_cast<const uint4*>(xr + (int64_t)m * A.K + 16 * j)[1];
+        const uint32_t w8[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          v[2 * i] = bf16_bits_to_f32(w8[i] & 0xffffu) * pre;
+          v[2 * i + 1] = bf16_bits_to_f32(w8[i] >> 16) * pre;
+        }
+        uint32_t lo[kTerms], hi[kTerms], code[kTerms];
+        block_terms(v, lo, hi, code);
+#pragma unroll
+        for (int t = 0; t < kTerms; ++t) {
+          const int n = t * A.M + m;
+          sts64(smem_u32(bsm) + b_offset(A.NB, n, 16 * j), lo[t], hi[t]);
+          sfb[((j >> 2) * A.NB + n) * 4 + (j & 3)] = (uint8_t)code[t];
+        }
+      }
+    }
+    fence_proxy_async_smem();  // the B operand is read by the tensor core (async proxy)
+    named_bar(1, pthreads);
+    if (warp >= 4 && ok) {
+      // B scales -> tensor memory: lane n % 32 of every subpartition, column kColSFB + 4 kb + n / 32
+      const int sub = warp - 4;
+      const uint32_t* words = reinterpret_cast<const uint32_t*>(base + A.smem_sfb);
+      const int ncol = nkb * 4;
+      for (int c0 = 0; c0 < ncol; c0 += 16) {
+        uint32_t v[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int c = c0 + i, kb = c >> 2, n = (c & 3) * 32 + lane;
+          v[i] = (c < ncol && n < A.NB) ? words[kb * A.NB + n] : 0u;
+        }
+        tc_st16(tmem + ((uint32_t)(32 * sub) << 16) + kColSFB + c0, v);
+      }
+      tc_wait_st();
+    }
+    tc_fence_before();
+    named_bar(1, pthreads);
+
+    if (warp == 1) {
+      // ---------------- MMA issue (one lane) ----------------
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t idesc = idesc_nvf4(A.NB);
+        const uint32_t bbase = smem_u32(base + A.smem_b);
+        for (int st = 0; st < nstages && ok; ++st) {
+          const int s = st % A.NS;
+          if (!mbar_wait_bounded(sfa0 + 8 * s, (uint32_t)((st / A.NS) & 1), A.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t astage = smem_u32(base) + (uint32_t)s * kStageBytes;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const int kb = st * 4 + j;
+            const uint64_t adesc = smem_desc_sw128(astage + 32u * j);
+            const uint64_t bdesc = smem_desc_sw128(bbase + (uint32_t)((kb >> 2) * A.NB * 128 + (kb & 3) * 32));
+            mma_nvf4(tmem + kColD, adesc, bdesc, idesc, tmem + kColSFA + 16u * s + 4u * j,
+                     tmem + kColSFB + 4u * (uint32_t)kb, kb > 0 ? 1u : 0u);
+          }
+          tc_commit(empty0 + 8 * s);
+        }
+        tc_commit(dfull);  // completes when every MMA issued above has finished
+      }
+      __syncwarp();
+    } else if (warp >= 4) {
+      // ---------------- stage scales -> tensor memory, then the epilogue ----------------
+      const int sub = warp - 4;
+      const uint32_t tsub = tmem + ((uint32_t)(32 * sub) << 16);
+      for (int st = 0; st < nstages && ok; ++st) {
+        const int s = st % A.NS;
+        if (!mbar_wait_bounded(full0 + 8 * s, (uint32_t)((st / A.NS) & 1), A.err)) { ok = false; break; }
+        // lane l holds rows l + 32c (c = 0..3); k-block j of the stage -> column 4j + c, bytes = its 4 scales
+        const uint8_t* srow = base + (size_t)s * kStageBytes + kStageA;
+        uint32_t w[4][4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 q = *reinterpret_cast<const uint4*>(srow + (lane + 32 * c) * 16);
+          w[c][0] = q.x; w[c][1] = q.y; w[c][2] = q.z; w[c][3] = q.w;
+        }
+        uint32_t v[16];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+#pragma unroll
+          for (int c = 0; c < 4; ++c) v[4 * j + c] = w[c][j];
+        tc_st16(tsub + kColSFA + 16u * s, v);
+        tc_wait_st();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sfa0 + 8 * s);
+      }
+      if (ok && !mbar_wait_bounded(dfull, 0, A.err)) ok = false;
+      tc_fence_after();
+      if (ok) {
+        const int row = row0 + 32 * sub + lane;
+        float accm[kMaxM];
+#pragma unroll
+        for (int m = 0; m < kMaxM; ++m) accm[m] = 0.f;
+        for (int c0 = 0; c0 < A.NB; c0 += 16) {
+          uint32_t d[16];
+          tc_ld16(tsub + kColD + c0, d);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            const int n = c0 + i, t = n / A.M, m = n - t * A.M;
+            if (t < kTerms) {
+              const uint32_t mb = amax_bits[m];
+              const int e0 = mb ? (int)(mb >> 23) - 127 : 0;
+              const int e = max(min(e0, 126), -126) - 2 * t;
+              const float f = e >= -126 ? __uint_as_float((uint32_t)(e + 127) << 23) : ldexpf(1.0f, e);
+#pragma unroll
+              for (int mm = 0; mm < kMaxM; ++mm)
+                if (mm == m) accm[mm] = fmaf(__uint_as_float(d[i]), f, accm[mm]);
+            }
+          }
+        }
+        if (row < A.N) {
+#pragma unroll
+          for (int m = 0; m < kMaxM; ++m)
+            if (m < A.M) store_out(A.out, A.out_dtype, (int64_t)m * A.out_stride + row, accm[m] * A.gs);
+        }
+      }
+      tc_fence_before();
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
+}  // namespace tc
+}  // namespace fp4x
