@@ -130,6 +130,21 @@ static int encode_rows_uncached(CUtensorMap* tm, const void* ptr, int64_t rows, 
   return FP4X_OK;
 }
 
+// [rows][row_bytes] u8 scale rows, box {16 bytes, 128 rows}, no swizzle (the tcgen05 NVFP4 kernel's scale tiles)
+static int encode_scale_rows(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t row_bytes) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(FP4X_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  const cuuint64_t gdim[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  const cuuint64_t gstride[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {16, 128};
+  const cuuint32_t es[2] = {1, 1};
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), gdim, gstride, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FP4X_ERR_UNSUPPORTED, "scale tensor map encode failed (" + std::to_string((int)r) + ")");
+  return FP4X_OK;
+}
+
 static int encode_rows(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t row_bytes, int inner) {
   struct Key {
     uintptr_t p;
@@ -446,6 +461,15 @@ static int check_rows(const void* p, int64_t row_bytes, const char* what) {
   return FP4X_OK;
 }
 
+template <int MT>
+static int launch_nv4_tc(const tc::Args& a, unsigned grid, int smem_total, void* stream) {
+  auto kern = tc::nv4_tc_kernel<MT>;
+  cudaError_t e = ensure_smem_attr((const void*)kern, smem_total);
+  if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
+  return check_launch(launch_pdl(kern, dim3(grid), dim3(tc::kThreads), (size_t)smem_total, (cudaStream_t)stream, a),
+                      "nv4 tcgen05 launch");
+}
+
 // NVFP4 on tcgen05 block-scaled MMAs (fp4x_tc.cuh): M <= 8 tokens, at least 64 row blocks of 128, K a multiple
 // of 256.  Returns 1 when the shape is not covered (the caller then uses the register-decode kernel).
 static int run_nv4_tc(const void* x, int64_t x_stride, const void* wp, const void* sc, float gs, void* out,
@@ -456,10 +480,7 @@ static int run_nv4_tc(const void* x, int64_t x_stride, const void* wp, const voi
   if (4 * (k / 64) > tc::kTmemCols - tc::kColSFB || NB > tc::kColSFA) return 1;
   if (!aligned(x, 16) || x_stride % 8 != 0 || x_stride < k || !aligned(wp, 16) || (k / 2) % 16 != 0) return 1;
   const int64_t lds = k / 16;
-  int scw = 0;
-  for (int w : {16, 8, 4})
-    if (lds % w == 0 && aligned(sc, w)) { scw = w; break; }
-  if (!scw || !out || out_stride < n) return 1;
+  if (lds % 16 != 0 || !aligned(sc, 16) || !out || out_stride < n) return 1;
   int rc;
   if ((rc = check_out_dtype(out_dtype))) return rc;
   tc::Args a;
@@ -467,7 +488,7 @@ static int run_nv4_tc(const void* x, int64_t x_stride, const void* wp, const voi
   const int b_bytes = (int)(k / 256) * NB * 128;
   const int xraw = round_up((int)(m * k * 2), 1024);
   const int sfb = round_up((int)(k / 64) * NB * 4, 1024);
-  const int fixed = b_bytes + xraw + sfb + 256 + 1024;
+  const int fixed = b_bytes + xraw + sfb + tc::kMiscBytes + 1024;
   int ns = (dv.smem_optin - fixed) / tc::kStageBytes;
   if (ns > tc::kMaxStages) ns = tc::kMaxStages;
   if (ns > (int)(k / tc::kKC)) ns = (int)(k / tc::kKC);
@@ -477,19 +498,25 @@ static int run_nv4_tc(const void* x, int64_t x_stride, const void* wp, const voi
   a.smem_xraw = a.smem_b + b_bytes;
   a.smem_sfb = a.smem_xraw + xraw;
   a.smem_misc = a.smem_sfb + sfb;
-  const int smem_total = a.smem_misc + 256 + 1024;
+  const int smem_total = a.smem_misc + tc::kMiscBytes + 1024;
   if ((rc = encode_rows(&a.tm, wp, n, k / 2, 128))) return rc;
+  if ((rc = encode_scale_rows(&a.tms, sc, n, k / 16))) return rc;
   a.x = (const __nv_bfloat16*)x; a.x_stride = x_stride;
-  a.sc = (const uint8_t*)sc; a.lds = lds; a.scw = scw;
+  a.sc = (const uint8_t*)sc; a.lds = lds; a.scw = 16;
   a.out = out; a.out_stride = out_stride; a.out_dtype = out_dtype; a.gs = gs;
   a.M = (int)m; a.N = (int)n; a.K = (int)k; a.NB = NB;
   a.err = dev_error_ptr();
-  cudaError_t e = ensure_smem_attr((const void*)tc::nv4_tc_kernel, smem_total);
-  if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
   const unsigned grid = (unsigned)((n + tc::kRows - 1) / tc::kRows);
-  return check_launch(launch_pdl(tc::nv4_tc_kernel, dim3(grid), dim3(tc::kThreads), (size_t)smem_total,
-                                 (cudaStream_t)stream, a),
-                      "nv4 tcgen05 launch");
+  switch (m) {
+    case 1: return launch_nv4_tc<1>(a, grid, smem_total, stream);
+    case 2: return launch_nv4_tc<2>(a, grid, smem_total, stream);
+    case 3: return launch_nv4_tc<3>(a, grid, smem_total, stream);
+    case 4: return launch_nv4_tc<4>(a, grid, smem_total, stream);
+    case 5: return launch_nv4_tc<5>(a, grid, smem_total, stream);
+    case 6: return launch_nv4_tc<6>(a, grid, smem_total, stream);
+    case 7: return launch_nv4_tc<7>(a, grid, smem_total, stream);
+    default: return launch_nv4_tc<8>(a, grid, smem_total, stream);
+  }
 }
 
 // shared path of the single-matrix GEMVs

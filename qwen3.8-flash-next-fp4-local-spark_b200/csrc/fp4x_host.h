@@ -65,6 +65,29 @@ cudaError_t launch_pdl_cluster(Kernel kernel, dim3 grid, dim3 block, size_t smem
   return e;
 }
 
+// the same with a thread-block cluster of (cluster_x, 1, 1) CTAs
+template <typename Kernel, typename... Args>
+cudaError_t launch_pdl_cluster_x(Kernel kernel, dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                                 int cluster_x, Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = (unsigned)cluster_x;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  const cudaError_t e = cudaLaunchKernelEx(&cfg, kernel, args...);
+  if (e == cudaSuccess) g_launches.fetch_add(1, std::memory_order_relaxed);
+  return e;
+}
+
 // address of the device error word on the current device (cudaGetSymbolAddress, cached per device)
 int* dev_error_ptr();
 

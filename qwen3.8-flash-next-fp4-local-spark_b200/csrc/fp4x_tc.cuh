@@ -16,10 +16,12 @@
 // range; after T = 6 terms the remainder is below 2^-13 of the token's largest element (the products themselves are
 // exact and accumulate in fp32).  The epilogue recombines the term columns with the factors 2^(e0 - 2t).
 //
-// Roles (256 threads): warp 0 streams weight tiles (TMA) and their scale bytes (cp.async); warp 1 owns the tensor
-// memory and one elected lane issues the MMAs; warps 4..7 (tensor-memory subpartitions 0..3) copy each stage's
-// scales into tensor memory and run the epilogue; warps 1..7 build the activation terms after the grid-dependency
-// wait.  Every wait is bounded; a failed wait records an error and the kernel still releases its tensor memory.
+// Roles (256 threads): warp 0 streams weight tiles and their scale tiles (TMA); warp 1 owns the tensor memory,
+// rearranges each stage's scales into the 32-row x 16-byte groups tcgen05.cp takes, and one of its lanes issues the
+// scale copies into tensor memory and the MMAs (the tensor core runs them in issue order); warps 1..7 build the
+// activation terms after the grid-dependency wait; warps 4..7 (tensor-memory subpartitions 0..3) write the
+// activation scales to tensor memory and run the epilogue.  Every wait is bounded; a failed wait records an error and
+// the kernel still releases its tensor memory.
 #pragma once
 #include <cuda.h>
 
@@ -31,18 +33,23 @@ namespace tc {
 constexpr int kThreads = 256;
 constexpr int kRows = 128;          // MMA M
 constexpr int kKC = 256;            // k per stage (128 bytes of e2m1 per row)
-constexpr int kMaxStages = 8;
+constexpr int kMaxStages = 12;
 constexpr int kTerms = 6;
 constexpr int kMaxM = 8;            // tokens: kTerms * 8 = 48 B columns
 constexpr int kTmemCols = 512;
 // tensor-memory column plan: accumulator, A scales (16 columns per stage), B scales (4 columns per 64-k block: the
 // B-scale tile is laid out for 128 columns of B whatever the MMA's N, so each k-block's slot starts 4-aligned)
-constexpr int kColD = 0, kColSFA = 128, kColSFB = 256;
+constexpr int kColD = 0, kColSFA = 64, kColSFB = 256;
+constexpr int kMiscBytes = 512;
 constexpr int kStageA = kRows * 128;                    // 16 KB of packed weights per stage
-constexpr int kStageBytes = kStageA + kRows * 16;       // + 16 scale bytes per row
+constexpr int kStageSc = kRows * 16;                    // the stage's scales as loaded: [128 rows][16 bytes]
+// + the same scales regrouped for tcgen05.cp: 4 groups (one per 64-k block) of [32 rows r][4 quarters q][4 scales]
+//   holding row 32q + r
+constexpr int kStageBytes = kStageA + 2 * kStageSc;
 
 struct Args {
   CUtensorMap tm;             // weights [N rows][K/2 bytes] u8, box {128 bytes, 64 rows}, 128-byte swizzle
+  CUtensorMap tms;            // scales [N rows][K/16 bytes] u8, box {16 bytes, 128 rows}, no swizzle
   const __nv_bfloat16* x;
   int64_t x_stride;
   const uint8_t* sc;          // e4m3 block scales [N][K/16]
@@ -75,6 +82,14 @@ FP4X_DEV void mma_nvf4(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint3
       "tcgen05.mma.cta_group::1.kind::mxf4nvf4.block_scale.block16 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
       "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
       : "memory");
+}
+// no-swizzle K-major descriptor of a [32 rows][16 bytes] group (8-row core matrices 128 bytes apart)
+FP4X_DEV uint64_t smem_desc_sf(uint32_t addr) {
+  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)(128u >> 4) << 32) | ((uint64_t)1u << 46);
+}
+// shared -> tensor memory: 32 rows x 128 bits into lanes 0..31 of every subpartition, 4 columns
+FP4X_DEV void tc_cp_sf(uint32_t taddr, uint64_t desc) {
+  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(taddr), "l"(desc) : "memory");
 }
 FP4X_DEV void tc_commit(uint32_t bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar) : "memory");
@@ -117,32 +132,43 @@ FP4X_DEV uint32_t e4m3_code_ceil(float v) {
   return c;
 }
 
-// One 16-element block of token m: the kTerms e2m1 terms (8 bytes each) and their scale codes.
+// One 16-element block of a token: the kTerms e2m1 terms (8 bytes each) and their scale codes.  v holds the
+// unscaled residual r; term t quantizes 4^t r (the factor keeps the scales inside e4m3's range) and removes
+// q S / 4^t from r.  The reciprocal only steers the choice of q; the residual uses the exact product q S.
 FP4X_DEV void block_terms(float (&v)[16], uint32_t (&lo)[kTerms], uint32_t (&hi)[kTerms], uint32_t (&code)[kTerms]) {
+  float up = 1.0f;  // 4^t
 #pragma unroll
   for (int t = 0; t < kTerms; ++t) {
-    float amax = 0.f;
+    float m0 = fmaxf(fabsf(v[0]), fabsf(v[1])), m1 = fmaxf(fabsf(v[2]), fabsf(v[3]));
+    float m2 = fmaxf(fabsf(v[4]), fabsf(v[5])), m3 = fmaxf(fabsf(v[6]), fabsf(v[7]));
 #pragma unroll
-    for (int i = 0; i < 16; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    for (int i = 8; i < 16; i += 4) {
+      m0 = fmaxf(m0, fabsf(v[i])); m1 = fmaxf(m1, fabsf(v[i + 1]));
+      m2 = fmaxf(m2, fabsf(v[i + 2])); m3 = fmaxf(m3, fabsf(v[i + 3]));
+    }
+    const float amax = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * up;
     uint32_t c = 0;
-    float s = 0.f, inv = 0.f;
+    float s_down = 0.f, inv_up = 0.f;
     if (amax > 0.f) {
       c = e4m3_code_ceil(amax * (1.0f / 6.0f));
-      s = e4m3_to_f32(c);
-      inv = 1.0f / s;
+      const float s = e4m3_to_f32(c);
+      float r;
+      asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
+      inv_up = r * up;
+      s_down = s * (1.0f / up);
     }
     code[t] = c;
     uint32_t b[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      b[i] = f32x2_to_e2m1x2(v[2 * i] * inv, v[2 * i + 1] * inv);
+      b[i] = f32x2_to_e2m1x2(v[2 * i] * inv_up, v[2 * i + 1] * inv_up);
       const uint32_t h = e2m1x2_to_f16x2(b[i]);
-      const float q0 = f16_bits_to_f32(h & 0xffffu), q1 = f16_bits_to_f32(h >> 16);
-      v[2 * i] = 4.0f * fmaf(-q0, s, v[2 * i]);
-      v[2 * i + 1] = 4.0f * fmaf(-q1, s, v[2 * i + 1]);
+      v[2 * i] = fmaf(-f16_bits_to_f32(h & 0xffffu), s_down, v[2 * i]);
+      v[2 * i + 1] = fmaf(-f16_bits_to_f32(h >> 16), s_down, v[2 * i + 1]);
     }
     lo[t] = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
     hi[t] = b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24);
+    up *= 4.0f;
   }
 }
 
@@ -153,7 +179,9 @@ FP4X_DEV uint32_t b_offset(int NB, int n, int k) {
   return (uint32_t)(slab * NB * 128 + (n >> 3) * 1024 + r * 128 + ((chunk ^ r) << 4) + (byte & 15));
 }
 
+template <int MT>
 __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_constant__ Args A) {
+  constexpr int NBT = (kTerms * MT + 15) / 16 * 16;
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -162,16 +190,15 @@ __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_consta
   const int nkb = A.K / 64;
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + A.smem_misc);
-  const uint32_t full0 = smem_u32(bars), sfa0 = full0 + 8 * kMaxStages, empty0 = sfa0 + 8 * kMaxStages;
+  const uint32_t full0 = smem_u32(bars), empty0 = full0 + 16 * kMaxStages;
   const uint32_t dfull = empty0 + 8 * kMaxStages, xbar = dfull + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + A.smem_misc + 8 * (3 * kMaxStages + 2));
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + A.smem_misc + 8 * (3 * kMaxStages + 3));
   uint32_t* amax_bits = tmem_slot + 1;          // [kMaxM] max |x| per token (float bits)
   volatile int* abort_flag = reinterpret_cast<volatile int*>(amax_bits + kMaxM);
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < A.NS; ++s) {
-      mbar_init(full0 + 8 * s, 33);
-      mbar_init(sfa0 + 8 * s, 4);
+      mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
     mbar_init(dfull, 1);
@@ -195,29 +222,18 @@ __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_consta
   if (warp == 0) {
     // ---------------- producer: weight tiles and their scale bytes (static: no grid-dependency wait) -----------
     pdl_launch_dependents();
-    const int words = 16 / A.scw;
     for (int st = 0; st < nstages && ok; ++st) {
       const int s = st % A.NS, round = st / A.NS;
       if (round > 0 && !mbar_wait_bounded(empty0 + 8 * s, (uint32_t)((round - 1) & 1), A.err)) { ok = false; break; }
       const uint32_t stage = smem_u32(base) + (uint32_t)s * kStageBytes;
       const int k0 = st * kKC;
       if (lane == 0) {
-        mbar_arrive_expect_tx(full0 + 8 * s, (uint32_t)kStageA);
+        mbar_arrive_expect_tx(full0 + 8 * s, (uint32_t)(kStageA + kStageSc));
         tma_load_2d(stage, &A.tm, k0 / 2, row0, full0 + 8 * s);
         tma_load_2d(stage + kStageA / 2, &A.tm, k0 / 2, row0 + 64, full0 + 8 * s);
+        tma_load_2d(stage + kStageA, &A.tms, k0 / 16, row0, full0 + 8 * s);
       }
-      for (int w = lane; w < kRows * words; w += 32) {
-        const int r = w / words, cw = w - r * words;
-        const int row = min(row0 + r, A.N - 1);
-        const uint8_t* src = A.sc + (int64_t)row * A.lds + k0 / 16 + cw * A.scw;
-        const uint32_t dst = stage + kStageA + r * 16 + cw * A.scw;
-        if (A.scw == 16) cp_async16(dst, src);
-        else if (A.scw == 8) cp_async8(dst, src);
-        else cp_async4(dst, src);
-      }
-      cp_async_arrive_noinc(full0 + 8 * s);
     }
-    asm volatile("cp.async.wait_all;" ::: "memory");
   } else {
     // ---------------- activations -> e2m1 terms (warps 1..7) ----------------
     const int ptid = threadIdx.x - 32, pthreads = kThreads - 32;
@@ -231,7 +247,7 @@ __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_consta
     }
     if (!mbar_wait_bounded(xbar, 0, A.err)) ok = false;
     if (ok) {
-      for (int m = 0; m < A.M; ++m) {
+      for (int m = 0; m < MT; ++m) {
         uint32_t mx = 0;
         for (int i = ptid; i < A.K / 8; i += pthreads) {
           const uint4 q = reinterpret_cast<const uint4*>(xr + (int64_t)m * A.K)[i];
@@ -252,7 +268,7 @@ __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_consta
       const int nblk = A.K / 16;
       uint8_t* bsm = base + A.smem_b;
       uint8_t* sfb = base + A.smem_sfb;
-      for (int idx = ptid; idx < A.M * nblk; idx += pthreads) {
+      for (int idx = ptid; idx < MT * nblk; idx += pthreads) {
         const int m = idx / nblk, j = idx - m * nblk;
         const uint32_t mb = amax_bits[m];
         // 2^-e0 with e0 the exponent of the token maximum (1 for an all-zero token)
@@ -271,9 +287,9 @@ __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_consta
         block_terms(v, lo, hi, code);
 #pragma unroll
         for (int t = 0; t < kTerms; ++t) {
-          const int n = t * A.M + m;
-          sts64(smem_u32(bsm) + b_offset(A.NB, n, 16 * j), lo[t], hi[t]);
-          sfb[((j >> 2) * A.NB + n) * 4 + (j & 3)] = (uint8_t)code[t];
+          const int n = t * MT + m;
+          sts64(smem_u32(bsm) + b_offset(NBT, n, 16 * j), lo[t], hi[t]);
+          sfb[((j >> 2) * NBT + n) * 4 + (j & 3)] = (uint8_t)code[t];
         }
       }
     }
@@ -289,7 +305,7 @@ __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_consta
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int c = c0 + i, kb = c >> 2, n = (c & 3) * 32 + lane;
-          v[i] = (c < ncol && n < A.NB) ? words[kb * A.NB + n] : 0u;
+          v[i] = (c < ncol && n < NBT) ? words[kb * NBT + n] : 0u;
         }
         tc_st16(tmem + ((uint32_t)(32 * sub) << 16) + kColSFB + c0, v);
       }
@@ -299,84 +315,77 @@ __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_consta
     named_bar(1, pthreads);
 
     if (warp == 1) {
-      // ---------------- MMA issue (one lane) ----------------
+      // ---------------- scale regrouping (whole warp) and MMA issue (lane 0) ----------------
       tc_fence_after();
-      if (lane == 0) {
-        const uint32_t idesc = idesc_nvf4(A.NB);
-        const uint32_t bbase = smem_u32(base + A.smem_b);
-        for (int st = 0; st < nstages && ok; ++st) {
-          const int s = st % A.NS;
-          if (!mbar_wait_bounded(sfa0 + 8 * s, (uint32_t)((st / A.NS) & 1), A.err)) { ok = false; break; }
+      const uint32_t idesc = idesc_nvf4(NBT);
+      const uint32_t bbase = smem_u32(base + A.smem_b);
+      for (int st = 0; st < nstages && ok; ++st) {
+        const int s = st % A.NS;
+        if (!mbar_wait_bounded(full0 + 8 * s, (uint32_t)((st / A.NS) & 1), A.err)) { ok = false; break; }
+        const uint32_t astage = smem_u32(base) + (uint32_t)s * kStageBytes;
+        // row r's 16 scale bytes (64-k blocks j = 0..3, four each) -> group j, line r % 32, word r / 32
+        const uint8_t* src = base + (size_t)s * kStageBytes + kStageA;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = lane + 32 * i;
+          const uint4 q = *reinterpret_cast<const uint4*>(src + r * 16);
+          const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            *reinterpret_cast<uint32_t*>(base + (size_t)s * kStageBytes + kStageA + kStageSc + j * 512 + (r & 31) * 16 +
+                                         (r >> 5) * 4) = w4[j];
+        }
+        fence_proxy_async_smem();  // tcgen05.cp reads the regrouped scales through the async proxy
+        __syncwarp();
+        if (lane == 0) {
           tc_fence_after();
-          const uint32_t astage = smem_u32(base) + (uint32_t)s * kStageBytes;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tc_cp_sf(tmem + kColSFA + 16u * s + 4u * j, smem_desc_sf(astage + kStageA + kStageSc + 512u * j));
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const int kb = st * 4 + j;
             const uint64_t adesc = smem_desc_sw128(astage + 32u * j);
-            const uint64_t bdesc = smem_desc_sw128(bbase + (uint32_t)((kb >> 2) * A.NB * 128 + (kb & 3) * 32));
+            const uint64_t bdesc = smem_desc_sw128(bbase + (uint32_t)((kb >> 2) * NBT * 128 + (kb & 3) * 32));
             mma_nvf4(tmem + kColD, adesc, bdesc, idesc, tmem + kColSFA + 16u * s + 4u * j,
                      tmem + kColSFB + 4u * (uint32_t)kb, kb > 0 ? 1u : 0u);
           }
           tc_commit(empty0 + 8 * s);
         }
-        tc_commit(dfull);  // completes when every MMA issued above has finished
+        __syncwarp();
       }
+      if (lane == 0) tc_commit(dfull);  // completes when every MMA issued above has finished
       __syncwarp();
     } else if (warp >= 4) {
-      // ---------------- stage scales -> tensor memory, then the epilogue ----------------
+      // ---------------- epilogue: row 32 sub + lane of the block, all B columns ----------------
       const int sub = warp - 4;
       const uint32_t tsub = tmem + ((uint32_t)(32 * sub) << 16);
-      for (int st = 0; st < nstages && ok; ++st) {
-        const int s = st % A.NS;
-        if (!mbar_wait_bounded(full0 + 8 * s, (uint32_t)((st / A.NS) & 1), A.err)) { ok = false; break; }
-        // lane l holds rows l + 32c (c = 0..3); k-block j of the stage -> column 4j + c, bytes = its 4 scales
-        const uint8_t* srow = base + (size_t)s * kStageBytes + kStageA;
-        uint32_t w[4][4];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint4 q = *reinterpret_cast<const uint4*>(srow + (lane + 32 * c) * 16);
-          w[c][0] = q.x; w[c][1] = q.y; w[c][2] = q.z; w[c][3] = q.w;
-        }
-        uint32_t v[16];
-#pragma unroll
-        for (int j = 0; j < 4; ++j)
-#pragma unroll
-          for (int c = 0; c < 4; ++c) v[4 * j + c] = w[c][j];
-        tc_st16(tsub + kColSFA + 16u * s, v);
-        tc_wait_st();
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(sfa0 + 8 * s);
-      }
       if (ok && !mbar_wait_bounded(dfull, 0, A.err)) ok = false;
       tc_fence_after();
       if (ok) {
-        const int row = row0 + 32 * sub + lane;
-        float accm[kMaxM];
+        uint32_t d[NBT];
 #pragma unroll
-        for (int m = 0; m < kMaxM; ++m) accm[m] = 0.f;
-        for (int c0 = 0; c0 < A.NB; c0 += 16) {
-          uint32_t d[16];
-          tc_ld16(tsub + kColD + c0, d);
-          tc_wait_ld();
+        for (int c0 = 0; c0 < NBT; c0 += 16) {
+          uint32_t q[16];
+          tc_ld16(tsub + kColD + c0, q);
 #pragma unroll
-          for (int i = 0; i < 16; ++i) {
-            const int n = c0 + i, t = n / A.M, m = n - t * A.M;
-            if (t < kTerms) {
-              const uint32_t mb = amax_bits[m];
-              const int e0 = mb ? (int)(mb >> 23) - 127 : 0;
-              const int e = max(min(e0, 126), -126) - 2 * t;
-              const float f = e >= -126 ? __uint_as_float((uint32_t)(e + 127) << 23) : ldexpf(1.0f, e);
-#pragma unroll
-              for (int mm = 0; mm < kMaxM; ++mm)
-                if (mm == m) accm[mm] = fmaf(__uint_as_float(d[i]), f, accm[mm]);
-            }
-          }
+          for (int i = 0; i < 16; ++i) d[c0 + i] = q[i];
         }
+        tc_wait_ld();
+        const int row = row0 + 32 * sub + lane;
         if (row < A.N) {
 #pragma unroll
-          for (int m = 0; m < kMaxM; ++m)
-            if (m < A.M) store_out(A.out, A.out_dtype, (int64_t)m * A.out_stride + row, accm[m] * A.gs);
+          for (int m = 0; m < MT; ++m) {
+            // column t * MT + m holds the term t products, scaled by 2^-e0 4^t: add the small terms first
+            float acc = 0.f;
+#pragma unroll
+            for (int t = kTerms - 1; t >= 0; --t)
+              acc = fmaf(__uint_as_float(d[t * MT + m]), __uint_as_float((uint32_t)(127 - 2 * t) << 23), acc);
+            const uint32_t mb = amax_bits[m];
+            const int e0 = max(min(mb ? (int)(mb >> 23) - 127 : 0, 126), -126);
+            acc *= __uint_as_float((uint32_t)(e0 + 127) << 23);
+            store_out(A.out, A.out_dtype, (int64_t)m * A.out_stride + row, acc * A.gs);
+          }
         }
       }
       tc_fence_before();
