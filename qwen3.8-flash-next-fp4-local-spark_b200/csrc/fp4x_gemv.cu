@@ -475,7 +475,9 @@ static int launch_nv4_tc(const tc::Args& a, unsigned grid, int smem_total, void*
 static int run_nv4_tc(const void* x, int64_t x_stride, const void* wp, const void* sc, float gs, void* out,
                       int64_t out_stride, int out_dtype, int64_t m, int64_t n, int64_t k, void* stream) {
   const DeviceFacts& dv = device_facts();
-  if (m < 1 || m > tc::kMaxM || k % tc::kKC != 0 || n < 64 * tc::kRows || n > (1 << 30)) return 1;
+  if (m < 1 || m > tc::kMaxM || k % tc::kKC != 0 || k / tc::kKC > tc::kMaxSlabs || n < 64 * tc::kRows ||
+      n > (1 << 30))
+    return 1;
   const int NB = (tc::kTerms * (int)m + 15) / 16 * 16;
   if (4 * (k / 64) > tc::kTmemCols - tc::kColSFB || NB > tc::kColSFA) return 1;
   if (!aligned(x, 16) || x_stride % 8 != 0 || x_stride < k || !aligned(wp, 16) || (k / 2) % 16 != 0) return 1;
@@ -487,7 +489,7 @@ static int run_nv4_tc(const void* x, int64_t x_stride, const void* wp, const voi
   std::memset(&a, 0, sizeof(a));
   const int b_bytes = (int)(k / 256) * NB * 128;
   const int xraw = round_up((int)(m * k * 2), 1024);
-  const int sfb = round_up((int)(k / 64) * NB * 4, 1024);
+  const int sfb = round_up((int)(k / 64) * 512, 1024);  // B scales in tcgen05.cp groups, one per 64-k block
   const int fixed = b_bytes + xraw + sfb + tc::kMiscBytes + 1024;
   int ns = (dv.smem_optin - fixed) / tc::kStageBytes;
   if (ns > tc::kMaxStages) ns = tc::kMaxStages;

@@ -16,12 +16,12 @@
 // range; after T = 6 terms the remainder is below 2^-13 of the token's largest element (the products themselves are
 // exact and accumulate in fp32).  The epilogue recombines the term columns with the factors 2^(e0 - 2t).
 //
-// Roles (256 threads): warp 0 streams weight tiles and their scale tiles (TMA); warp 1 owns the tensor memory,
-// rearranges each stage's scales into the 32-row x 16-byte groups tcgen05.cp takes, and one of its lanes issues the
-// scale copies into tensor memory and the MMAs (the tensor core runs them in issue order); warps 1..7 build the
-// activation terms after the grid-dependency wait; warps 4..7 (tensor-memory subpartitions 0..3) write the
-// activation scales to tensor memory and run the epilogue.  Every wait is bounded; a failed wait records an error and
-// the kernel still releases its tensor memory.
+// Roles (384 threads): warp 0 streams weight tiles and their scale tiles (TMA); warp 1 owns the tensor memory and
+// one of its lanes issues the MMAs; warps 2..7 turn the activations into e2m1 terms after the grid-dependency wait,
+// slab by slab (256 k), so the MMAs of the first slabs start while later slabs are still being prepared; warps 8..11
+// (tensor-memory subpartitions 0..3) write each stage's A scales and each slab's B scales into tensor memory from
+// registers, running ahead of the MMAs, and then run the epilogue.  Every wait is bounded; a failed wait records an
+// error and the kernel still releases its tensor memory.
 #pragma once
 #include <cuda.h>
 
@@ -30,22 +30,23 @@
 namespace fp4x {
 namespace tc {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 384;
 constexpr int kRows = 128;          // MMA M
 constexpr int kKC = 256;            // k per stage (128 bytes of e2m1 per row)
-constexpr int kMaxStages = 12;
+constexpr int kMaxStages = 8;
+constexpr int kMaxSlabs = 16;       // 256-k activation slabs: K <= 4096
 constexpr int kTerms = 6;
 constexpr int kMaxM = 8;            // tokens: kTerms * 8 = 48 B columns
 constexpr int kTmemCols = 512;
-// tensor-memory column plan: accumulator, A scales (16 columns per stage), B scales (4 columns per 64-k block: the
-// B-scale tile is laid out for 128 columns of B whatever the MMA's N, so each k-block's slot starts 4-aligned)
-constexpr int kColD = 0, kColSFA = 64, kColSFB = 256;
+// tensor-memory column plan: accumulators, A scales (16 columns per stage), B scales (4 columns per 64-k block: the
+// B-scale tile is laid out for 128 columns of B whatever the MMA's N, so each k-block's slot starts 4-aligned).
+// Consecutive 64-k blocks accumulate into different accumulators (kb mod NACC): MMAs into one accumulator run one
+// after the other, and at these small N their latency, not their arithmetic, would set the pace.
+constexpr int kColD = 0, kColSFA = 128, kColSFB = 256;
 constexpr int kMiscBytes = 512;
 constexpr int kStageA = kRows * 128;                    // 16 KB of packed weights per stage
 constexpr int kStageSc = kRows * 16;                    // the stage's scales as loaded: [128 rows][16 bytes]
-// + the same scales regrouped for tcgen05.cp: 4 groups (one per 64-k block) of [32 rows r][4 quarters q][4 scales]
-//   holding row 32q + r
-constexpr int kStageBytes = kStageA + 2 * kStageSc;
+constexpr int kStageBytes = kStageA + kStageSc;         // 18 KB, a multiple of 1024
 
 struct Args {
   CUtensorMap tm;             // weights [N rows][K/2 bytes] u8, box {128 bytes, 64 rows}, 128-byte swizzle
@@ -182,29 +183,33 @@ FP4X_DEV uint32_t b_offset(int NB, int n, int k) {
 template <int MT>
 __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_constant__ Args A) {
   constexpr int NBT = (kTerms * MT + 15) / 16 * 16;
+  constexpr int NACC = NBT <= 32 ? 4 : 2;  // accumulators of NBT columns within the 128 columns at kColD
+  constexpr int kBlkPerSlab = MT * 16;     // 16-element activation blocks per 256-k slab (all tokens)
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int row0 = blockIdx.x * kRows;
-  const int nstages = A.K / kKC;
-  const int nkb = A.K / 64;
+  const int nstages = A.K / kKC;  // = activation slabs
 
   uint64_t* bars = reinterpret_cast<uint64_t*>(base + A.smem_misc);
-  const uint32_t full0 = smem_u32(bars), empty0 = full0 + 16 * kMaxStages;
-  const uint32_t dfull = empty0 + 8 * kMaxStages, xbar = dfull + 8;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + A.smem_misc + 8 * (3 * kMaxStages + 3));
-  uint32_t* amax_bits = tmem_slot + 1;          // [kMaxM] max |x| per token (float bits)
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(amax_bits + kMaxM);
+  const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * kMaxStages, slab0 = empty0 + 8 * kMaxStages;
+  const uint32_t sfr0 = slab0 + 8 * kMaxSlabs;  // [kMaxSlabs] A and B scales of the stage are in tensor memory
+  const uint32_t dfull = sfr0 + 8 * kMaxSlabs, xbar = dfull + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + A.smem_misc + 8 * (2 * kMaxStages + 2 * kMaxSlabs + 2));
+  uint32_t* amax_bits = tmem_slot + 1;  // [kMaxM] max |x| per token (float bits)
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < A.NS; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
     }
+    for (int s = 0; s < nstages; ++s) {
+      mbar_init(slab0 + 8 * s, kBlkPerSlab);
+      mbar_init(sfr0 + 8 * s, 4);
+    }
     mbar_init(dfull, 1);
     mbar_init(xbar, 1);
     for (int m = 0; m < kMaxM; ++m) amax_bits[m] = 0u;
-    *abort_flag = 0;
     mbar_init_fence();
   }
   if (warp == 1) {
@@ -220,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_consta
   bool ok = true;
 
   if (warp == 0) {
-    // ---------------- producer: weight tiles and their scale bytes (static: no grid-dependency wait) -----------
+    // ---------------- producer: weight tiles and their scale tiles (static: no grid-dependency wait) -----------
     pdl_launch_dependents();
     for (int st = 0; st < nstages && ok; ++st) {
       const int s = st % A.NS, round = st / A.NS;
@@ -234,15 +239,110 @@ __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_consta
         tma_load_2d(stage + kStageA, &A.tms, k0 / 16, row0, full0 + 8 * s);
       }
     }
+  } else if (warp == 1) {
+    // ---------------- MMA issue (lane 0) ----------------
+    if (lane == 0) {
+      const uint32_t idesc = idesc_nvf4(NBT);
+      const uint32_t bbase = smem_u32(base + A.smem_b);
+      for (int st = 0; st < nstages && ok; ++st) {
+        const int s = st % A.NS;
+        // the scale writers have seen this stage's tiles land and this slab's terms done
+        if (!mbar_wait_bounded(sfr0 + 8 * st, 0, A.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t astage = smem_u32(base) + (uint32_t)s * kStageBytes;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int kb = st * 4 + j;
+          const uint64_t adesc = smem_desc_sw128(astage + 32u * j);
+          const uint64_t bdesc = smem_desc_sw128(bbase + (uint32_t)((kb >> 2) * NBT * 128 + (kb & 3) * 32));
+          mma_nvf4(tmem + kColD + (uint32_t)((kb % NACC) * NBT), adesc, bdesc, idesc,
+                   tmem + kColSFA + 16u * s + 4u * j, tmem + kColSFB + 4u * (uint32_t)kb, kb >= NACC ? 1u : 0u);
+        }
+        tc_commit(empty0 + 8 * s);
+      }
+      tc_commit(dfull);  // completes when every MMA issued above has finished
+    }
+    __syncwarp();
+  } else if (warp >= 8) {
+    // ---------------- scale writers (subpartition warp - 8), then the epilogue ----------------
+    const int sub = warp - 8;
+    const uint32_t tsub = tmem + ((uint32_t)(32 * sub) << 16);
+    const uint8_t* sfb = base + A.smem_sfb;
+    for (int st = 0; st < nstages && ok; ++st) {
+      const int s = st % A.NS;
+      if (!mbar_wait_bounded(full0 + 8 * s, (uint32_t)((st / A.NS) & 1), A.err)) { ok = false; break; }
+      // A: lane l holds rows l + 32c (c = 0..3); 64-k block j of the stage -> column 4j + c
+      const uint8_t* srow = base + (size_t)s * kStageBytes + kStageA;
+      uint32_t w[4][4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const uint4 q = *reinterpret_cast<const uint4*>(srow + (lane + 32 * c) * 16);
+        w[c][0] = q.x; w[c][1] = q.y; w[c][2] = q.z; w[c][3] = q.w;
+      }
+      uint32_t va[16];
+#pragma unroll
+      for (int j = 0; j < 4; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c) va[4 * j + c] = w[c][j];
+      tc_st16(tsub + kColSFA + 16u * s, va);
+      // B: this slab's 4 k-blocks, column 4 kb + n / 32 holds the scales of B column n (lane n % 32)
+      if (!mbar_wait_bounded(slab0 + 8 * st, 0, A.err)) { ok = false; break; }
+      uint32_t vb[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int kb = st * 4 + (i >> 2), c = i & 3;
+        vb[i] = 32 * c < NBT ? *reinterpret_cast<const uint32_t*>(sfb + kb * 512 + lane * 16 + c * 4) : 0u;
+      }
+      tc_st16(tsub + kColSFB + 16u * st, vb);
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sfr0 + 8 * st);
+    }
+    // ---------------- epilogue: row 32 sub + lane of the block, all B columns ----------------
+    if (ok && !mbar_wait_bounded(dfull, 0, A.err)) ok = false;
+    tc_fence_after();
+    if (ok) {
+      float d[NBT];
+#pragma unroll
+      for (int i = 0; i < NBT; ++i) d[i] = 0.f;
+#pragma unroll
+      for (int a = 0; a < NACC; ++a) {
+#pragma unroll
+        for (int c0 = 0; c0 < NBT; c0 += 16) {
+          uint32_t q[16];
+          tc_ld16(tsub + kColD + (uint32_t)(a * NBT + c0), q);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) d[c0 + i] += __uint_as_float(q[i]);
+        }
+      }
+      const int row = row0 + 32 * sub + lane;
+      if (row < A.N) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          // column t * MT + m holds the term t products, scaled by 2^-e0 4^t: add the small terms first
+          float acc = 0.f;
+#pragma unroll
+          for (int t = kTerms - 1; t >= 0; --t)
+            acc = fmaf(d[t * MT + m], __uint_as_float((uint32_t)(127 - 2 * t) << 23), acc);
+          const uint32_t mb = amax_bits[m];
+          const int e0 = max(min(mb ? (int)(mb >> 23) - 127 : 0, 126), -126);
+          acc *= __uint_as_float((uint32_t)(e0 + 127) << 23);
+          store_out(A.out, A.out_dtype, (int64_t)m * A.out_stride + row, acc * A.gs);
+        }
+      }
+    }
+    tc_fence_before();
   } else {
-    // ---------------- activations -> e2m1 terms (warps 1..7) ----------------
-    const int ptid = threadIdx.x - 32, pthreads = kThreads - 32;
+    // ---------------- activations -> e2m1 terms (warps 2..7), slab by slab ----------------
+    const int ptid = threadIdx.x - 64, pthreads = 192;
     pdl_wait();
     const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(base + A.smem_xraw);
     if (ptid == 0) {
       const uint32_t bytes = (uint32_t)A.K * 2u;
-      mbar_arrive_expect_tx(xbar, bytes * (uint32_t)A.M);
-      for (int m = 0; m < A.M; ++m)
+      mbar_arrive_expect_tx(xbar, bytes * (uint32_t)MT);
+      for (int m = 0; m < MT; ++m)
         bulk_g2s(smem_u32(base + A.smem_xraw) + m * bytes, A.x + (int64_t)m * A.x_stride, bytes, xbar);
     }
     if (!mbar_wait_bounded(xbar, 0, A.err)) ok = false;
@@ -264,12 +364,13 @@ __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_consta
       }
     }
     named_bar(1, pthreads);
-    if (ok) {
-      const int nblk = A.K / 16;
-      uint8_t* bsm = base + A.smem_b;
-      uint8_t* sfb = base + A.smem_sfb;
-      for (int idx = ptid; idx < MT * nblk; idx += pthreads) {
-        const int m = idx / nblk, j = idx - m * nblk;
+    // blocks in slab-major order (slab, token, block of the slab), so the first slabs are done first
+    uint8_t* bsm = base + A.smem_b;
+    uint8_t* sfb = base + A.smem_sfb;
+    for (int idx = ptid; idx < nstages * kBlkPerSlab; idx += pthreads) {
+      const int slab = idx / kBlkPerSlab, rem = idx - slab * kBlkPerSlab;
+      const int m = rem >> 4, j = slab * 16 + (rem & 15);
+      if (ok) {
         const uint32_t mb = amax_bits[m];
         // 2^-e0 with e0 the exponent of the token maximum (1 for an all-zero token)
         const int e0 = mb ? (int)(mb >> 23) - 127 : 0;
@@ -289,106 +390,12 @@ __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_consta
         for (int t = 0; t < kTerms; ++t) {
           const int n = t * MT + m;
           sts64(smem_u32(bsm) + b_offset(NBT, n, 16 * j), lo[t], hi[t]);
-          sfb[((j >> 2) * NBT + n) * 4 + (j & 3)] = (uint8_t)code[t];
+          // B scales in the tcgen05.cp grouping: group kb, line n % 32, word n / 32, byte j % 4
+          sfb[(j >> 2) * 512 + (n & 31) * 16 + (n >> 5) * 4 + (j & 3)] = (uint8_t)code[t];
         }
       }
-    }
-    fence_proxy_async_smem();  // the B operand is read by the tensor core (async proxy)
-    named_bar(1, pthreads);
-    if (warp >= 4 && ok) {
-      // B scales -> tensor memory: lane n % 32 of every subpartition, column kColSFB + 4 kb + n / 32
-      const int sub = warp - 4;
-      const uint32_t* words = reinterpret_cast<const uint32_t*>(base + A.smem_sfb);
-      const int ncol = nkb * 4;
-      for (int c0 = 0; c0 < ncol; c0 += 16) {
-        uint32_t v[16];
-#pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const int c = c0 + i, kb = c >> 2, n = (c & 3) * 32 + lane;
-          v[i] = (c < ncol && n < NBT) ? words[kb * NBT + n] : 0u;
-        }
-        tc_st16(tmem + ((uint32_t)(32 * sub) << 16) + kColSFB + c0, v);
-      }
-      tc_wait_st();
-    }
-    tc_fence_before();
-    named_bar(1, pthreads);
-
-    if (warp == 1) {
-      // ---------------- scale regrouping (whole warp) and MMA issue (lane 0) ----------------
-      tc_fence_after();
-      const uint32_t idesc = idesc_nvf4(NBT);
-      const uint32_t bbase = smem_u32(base + A.smem_b);
-      for (int st = 0; st < nstages && ok; ++st) {
-        const int s = st % A.NS;
-        if (!mbar_wait_bounded(full0 + 8 * s, (uint32_t)((st / A.NS) & 1), A.err)) { ok = false; break; }
-        const uint32_t astage = smem_u32(base) + (uint32_t)s * kStageBytes;
-        // row r's 16 scale bytes (64-k blocks j = 0..3, four each) -> group j, line r % 32, word r / 32
-        const uint8_t* src = base + (size_t)s * kStageBytes + kStageA;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int r = lane + 32 * i;
-          const uint4 q = *reinterpret_cast<const uint4*>(src + r * 16);
-          const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            *reinterpret_cast<uint32_t*>(base + (size_t)s * kStageBytes + kStageA + kStageSc + j * 512 + (r & 31) * 16 +
-                                         (r >> 5) * 4) = w4[j];
-        }
-        fence_proxy_async_smem();  // tcgen05.cp reads the regrouped scales through the async proxy
-        __syncwarp();
-        if (lane == 0) {
-          tc_fence_after();
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-            tc_cp_sf(tmem + kColSFA + 16u * s + 4u * j, smem_desc_sf(astage + kStageA + kStageSc + 512u * j));
-#pragma unroll
-          for (int j = 0; j < 4; ++j) {
-            const int kb = st * 4 + j;
-            const uint64_t adesc = smem_desc_sw128(astage + 32u * j);
-            const uint64_t bdesc = smem_desc_sw128(bbase + (uint32_t)((kb >> 2) * NBT * 128 + (kb & 3) * 32));
-            mma_nvf4(tmem + kColD, adesc, bdesc, idesc, tmem + kColSFA + 16u * s + 4u * j,
-                     tmem + kColSFB + 4u * (uint32_t)kb, kb > 0 ? 1u : 0u);
-          }
-          tc_commit(empty0 + 8 * s);
-        }
-        __syncwarp();
-      }
-      if (lane == 0) tc_commit(dfull);  // completes when every MMA issued above has finished
-      __syncwarp();
-    } else if (warp >= 4) {
-      // ---------------- epilogue: row 32 sub + lane of the block, all B columns ----------------
-      const int sub = warp - 4;
-      const uint32_t tsub = tmem + ((uint32_t)(32 * sub) << 16);
-      if (ok && !mbar_wait_bounded(dfull, 0, A.err)) ok = false;
-      tc_fence_after();
-      if (ok) {
-        uint32_t d[NBT];
-#pragma unroll
-        for (int c0 = 0; c0 < NBT; c0 += 16) {
-          uint32_t q[16];
-          tc_ld16(tsub + kColD + c0, q);
-#pragma unroll
-          for (int i = 0; i < 16; ++i) d[c0 + i] = q[i];
-        }
-        tc_wait_ld();
-        const int row = row0 + 32 * sub + lane;
-        if (row < A.N) {
-#pragma unroll
-          for (int m = 0; m < MT; ++m) {
-            // column t * MT + m holds the term t products, scaled by 2^-e0 4^t: add the small terms first
-            float acc = 0.f;
-#pragma unroll
-            for (int t = kTerms - 1; t >= 0; --t)
-              acc = fmaf(__uint_as_float(d[t * MT + m]), __uint_as_float((uint32_t)(127 - 2 * t) << 23), acc);
-            const uint32_t mb = amax_bits[m];
-            const int e0 = max(min(mb ? (int)(mb >> 23) - 127 : 0, 126), -126);
-            acc *= __uint_as_float((uint32_t)(e0 + 127) << 23);
-            store_out(A.out, A.out_dtype, (int64_t)m * A.out_stride + row, acc * A.gs);
-          }
-        }
-      }
-      tc_fence_before();
+      fence_proxy_async_smem();  // the tensor core reads the terms and scales through the async proxy
+      mbar_arrive(slab0 + 8 * slab);
     }
   }
   __syncthreads();
