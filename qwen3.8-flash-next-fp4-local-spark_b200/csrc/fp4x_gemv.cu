@@ -130,13 +130,13 @@ static int encode_rows_uncached(CUtensorMap* tm, const void* ptr, int64_t rows, 
   return FP4X_OK;
 }
 
-// [rows][row_bytes] u8 scale rows, box {16 bytes, 128 rows}, no swizzle (the tcgen05 NVFP4 kernel's scale tiles)
-static int encode_scale_rows(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t row_bytes) {
+// [rows][row_bytes] u8 scale rows, box {box_bytes, 128 rows}, no swizzle (the tcgen05 kernels' scale tiles)
+static int encode_scale_box(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t row_bytes, int box_bytes) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(FP4X_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
   const cuuint64_t gdim[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
   const cuuint64_t gstride[1] = {(cuuint64_t)row_bytes};
-  const cuuint32_t box[2] = {16, 128};
+  const cuuint32_t box[2] = {(cuuint32_t)box_bytes, 128};
   const cuuint32_t es[2] = {1, 1};
   CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), gdim, gstride, box, es,
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -502,7 +502,7 @@ static int run_nv4_tc(const void* x, int64_t x_stride, const void* wp, const voi
   a.smem_misc = a.smem_sfb + sfb;
   const int smem_total = a.smem_misc + tc::kMiscBytes + 1024;
   if ((rc = encode_rows(&a.tm, wp, n, k / 2, 128))) return rc;
-  if ((rc = encode_scale_rows(&a.tms, sc, n, k / 16))) return rc;
+  if ((rc = encode_scale_box(&a.tms, sc, n, k / 16, 16))) return rc;
   a.x = (const __nv_bfloat16*)x; a.x_stride = x_stride;
   a.sc = (const uint8_t*)sc; a.lds = lds; a.scw = 16;
   a.out = out; a.out_stride = out_stride; a.out_dtype = out_dtype; a.gs = gs;
@@ -518,6 +518,67 @@ static int run_nv4_tc(const void* x, int64_t x_stride, const void* wp, const voi
     case 6: return launch_nv4_tc<6>(a, grid, smem_total, stream);
     case 7: return launch_nv4_tc<7>(a, grid, smem_total, stream);
     default: return launch_nv4_tc<8>(a, grid, smem_total, stream);
+  }
+}
+
+template <int MT>
+static int launch_mx8_tc(const tc::MxArgs& a, unsigned grid, int smem_total, void* stream) {
+  auto kern = tc::mx8_tc_kernel<MT>;
+  cudaError_t e = ensure_smem_attr((const void*)kern, smem_total);
+  if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
+  return check_launch(launch_pdl(kern, dim3(grid), dim3(tc::kThreads), (size_t)smem_total, (cudaStream_t)stream, a),
+                      "mx8 tcgen05 launch");
+}
+
+// MXFP8 on tcgen05 block-scaled MMAs (fp4x_tc.cuh): M <= 8 tokens, at least 64 row blocks of 128, K a multiple of
+// 512 up to 4096.  Returns 1 when the shape is not covered (the caller then uses the register-decode kernel).
+static int run_mx8_tc(const void* x, int64_t x_stride, const void* w, const void* sc, void* out, int64_t out_stride,
+                      int out_dtype, int64_t m, int64_t n, int64_t k, void* stream) {
+  const DeviceFacts& dv = device_facts();
+  if (m < 1 || m > tc::kMaxM || k % 512 != 0 || k / tc::kMxKC > tc::kMxMaxChunks || n < 64 * tc::kRows ||
+      n > (1 << 30))
+    return 1;
+  if (!aligned(x, 16) || x_stride % 8 != 0 || x_stride < k || !aligned(w, 16) || !aligned(sc, 16) || !out ||
+      out_stride < n)
+    return 1;
+  int rc;
+  if ((rc = check_out_dtype(out_dtype))) return rc;
+  const int NB = (tc::kMxTerms * (int)m + 15) / 16 * 16;
+  tc::MxArgs a;
+  std::memset(&a, 0, sizeof(a));
+  const int b_bytes = (int)(k / tc::kMxKC) * NB * 128;
+  const int xraw = round_up((int)(m * k * 2), 1024);
+  const int sfb = round_up((int)(k / tc::kMxKC) * 512, 1024);
+  const int sfa = round_up(tc::kRows * (int)(k / 32), 1024);
+  const int misc = 1024;
+  const int fixed = b_bytes + xraw + sfb + sfa + misc + 1024;
+  int ns = (dv.smem_optin - fixed) / tc::kStageA;
+  if (ns > tc::kMxMaxStages) ns = tc::kMxMaxStages;
+  if (ns > (int)(k / tc::kMxKC)) ns = (int)(k / tc::kMxKC);
+  if (ns < 2) return 1;
+  a.NS = ns;
+  a.smem_b = ns * tc::kStageA;
+  a.smem_xraw = a.smem_b + b_bytes;
+  a.smem_sfb = a.smem_xraw + xraw;
+  a.smem_sfa = a.smem_sfb + sfb;
+  a.smem_misc = a.smem_sfa + sfa;
+  const int smem_total = a.smem_misc + misc + 1024;
+  if ((rc = encode_rows(&a.tm, w, n, k, 128))) return rc;
+  if ((rc = encode_scale_box(&a.tms, sc, n, k / 32, (int)(k / 32)))) return rc;
+  a.x = (const __nv_bfloat16*)x; a.x_stride = x_stride;
+  a.out = out; a.out_stride = out_stride; a.out_dtype = out_dtype;
+  a.M = (int)m; a.N = (int)n; a.K = (int)k;
+  a.err = dev_error_ptr();
+  const unsigned grid = (unsigned)((n + tc::kRows - 1) / tc::kRows);
+  switch (m) {
+    case 1: return launch_mx8_tc<1>(a, grid, smem_total, stream);
+    case 2: return launch_mx8_tc<2>(a, grid, smem_total, stream);
+    case 3: return launch_mx8_tc<3>(a, grid, smem_total, stream);
+    case 4: return launch_mx8_tc<4>(a, grid, smem_total, stream);
+    case 5: return launch_mx8_tc<5>(a, grid, smem_total, stream);
+    case 6: return launch_mx8_tc<6>(a, grid, smem_total, stream);
+    case 7: return launch_mx8_tc<7>(a, grid, smem_total, stream);
+    default: return launch_mx8_tc<8>(a, grid, smem_total, stream);
   }
 }
 
@@ -658,6 +719,8 @@ int fp4x_plan_describe(int fmt, int64_t m, int64_t n, int64_t k, int64_t batch, 
 int fp4x_mx8_linear(const void* x, int64_t x_stride, const void* w, const void* s, void* out, int64_t out_stride,
                     int out_dtype, int64_t m, int64_t n, int64_t k, void* ws, size_t ws_bytes, int32_t* counters,
                     int64_t n_counters, void* stream) {
+  const int rc = run_mx8_tc(x, x_stride, w, s, out, out_stride, out_dtype, m, n, k, stream);
+  if (rc <= 0) return rc;
   return run_gemv(FMT_MX8, x, x_stride, w, nullptr, s, 1.f, 16, out, nullptr, out_stride, out_dtype, m, n, k, ws,
                   ws_bytes, counters, n_counters, stream, EPI_STORE);
 }

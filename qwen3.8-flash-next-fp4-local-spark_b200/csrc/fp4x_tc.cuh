@@ -405,5 +405,281 @@ __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_consta
   }
 }
 
+// =====================================================================================================
+// MXFP8 GEMV on tcgen05 block-scaled MMAs (kind::mxf8f6f4, one e8m0 scale per 32 k):
+// out[m, n] = sum_k x[m, k] * e4m3(W[n, k]) * 2^(S[n, k / 32] - 127)  -- the reference's _mx8 (x/fp4x_kernels.py:9-29)
+//
+// Same pipeline as the NVFP4 kernel, with these differences.  A stage is 128 k (128 bytes of e4m3 per row) and one
+// MMA covers 32 k.  The e8m0 scales of the CTA's 128 rows are loaded once ([128][K/32] bytes, one TMA) and written
+// to tensor memory once: for the 128-k chunk c, lane r % 32 (every subpartition), column 4c + r / 32 holds row r's
+// four scales, and the MMA of the chunk's 32-k block j selects byte j (scale-factor id j).  The activation terms are
+// e4m3 with a power-of-two (e8m0) scale per 32-element block: S_t = 2^(e - 7) for the block's largest residual in
+// [2^e, 2^(e+1)), q_t = e4m3(r_t / S_t), r_{t+1} = r_t - q_t S_t.  Each term keeps 4 significant bits of every
+// element (e4m3 is exact below 2^8 S_t), so after 4 terms what is left is below 2^-15 of the block's largest element.
+// e8m0 covers every fp32 exponent, so no token-wide pre-scale is needed.
+// =====================================================================================================
+constexpr int kMxKC = 128;                 // k per stage
+constexpr int kMxTerms = 4;
+constexpr int kMxMaxStages = 12;
+constexpr int kMxMaxChunks = 32;           // 128-k chunks: K <= 4096
+constexpr int kMxColD = 0, kMxColSFA = 128, kMxColSFB = 256;  // SFA / SFB: 4 columns per 128-k chunk
+
+struct MxArgs {
+  CUtensorMap tm;             // weights [N rows][K bytes] e4m3, box {128 bytes, 64 rows}, 128-byte swizzle
+  CUtensorMap tms;            // scales [N rows][K/32 bytes] e8m0, box {K/32 bytes, 128 rows}, no swizzle
+  const __nv_bfloat16* x;
+  int64_t x_stride;
+  void* out;
+  int64_t out_stride;
+  int out_dtype;
+  int M, N, K;
+  int NS;
+  int smem_b, smem_xraw, smem_sfb, smem_sfa, smem_misc;
+  int* err;
+};
+
+FP4X_DEV uint32_t idesc_mxf8(int nb, uint32_t sf_id) {
+  // kind::mxf8f6f4: A, B e4m3 (0), K-major, N = nb, scales ue8m0, M = 128, K = 32, scale-factor ids (byte) sf_id
+  return (sf_id << 4) | ((uint32_t)(nb >> 3) << 17) | (1u << 23) | (8u << 24) | (sf_id << 29);
+}
+FP4X_DEV void mma_mxf8(uint32_t d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t sfa, uint32_t sfb, uint32_t acc) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale.block32 [%0], %1, %2, %3, [%5], [%6], p;\n\t}" ::"r"(d),
+      "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(sfa), "r"(sfb)
+      : "memory");
+}
+FP4X_DEV uint32_t f32x2_to_e4m3x2(float lo, float hi) {
+  uint16_t h;
+  asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(h) : "f"(hi), "f"(lo));
+  return h;
+}
+// byte offset of (B column n, k) in the 128-byte-swizzled K-major e4m3 B operand: slabs of 128 k, 8-column atoms
+FP4X_DEV uint32_t b_offset_mx(int NB, int n, int k) {
+  const int slab = k >> 7, byte = k & 127;
+  const int r = n & 7, chunk = byte >> 4;
+  return (uint32_t)(slab * NB * 128 + (n >> 3) * 1024 + r * 128 + ((chunk ^ r) << 4) + (byte & 15));
+}
+
+template <int MT>
+__global__ void __launch_bounds__(kThreads, 1) mx8_tc_kernel(const __grid_constant__ MxArgs A) {
+  constexpr int NBT = (kMxTerms * MT + 15) / 16 * 16;
+  constexpr int NACC = NBT <= 32 ? 4 : 2;
+  constexpr int kBlkPerSlab = MT * 4;  // 32-element activation blocks per 128-k slab (all tokens)
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int row0 = blockIdx.x * kRows;
+  const int nstages = A.K / kMxKC;  // = activation slabs = scale chunks
+  const int lds = A.K / 32;
+
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base + A.smem_misc);
+  const uint32_t full0 = smem_u32(bars), empty0 = full0 + 8 * kMxMaxStages, slab0 = empty0 + 8 * kMxMaxStages;
+  const uint32_t sfr0 = slab0 + 8 * kMxMaxChunks;
+  const uint32_t dfull = sfr0 + 8 * kMxMaxChunks, xbar = dfull + 8, sabar = xbar + 8;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(base + A.smem_misc + 8 * (2 * kMxMaxStages + 2 * kMxMaxChunks + 3));
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < A.NS; ++s) {
+      mbar_init(full0 + 8 * s, 1);
+      mbar_init(empty0 + 8 * s, 1);
+    }
+    for (int s = 0; s < nstages; ++s) {
+      mbar_init(slab0 + 8 * s, kBlkPerSlab);
+      mbar_init(sfr0 + 8 * s, 4);
+    }
+    mbar_init(dfull, 1);
+    mbar_init(xbar, 1);
+    mbar_init(sabar, 1);
+    mbar_init_fence();
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(kTmemCols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  bool ok = true;
+
+  if (warp == 0) {
+    // ---------------- producer: the CTA's scales once, then the weight tiles ----------------
+    pdl_launch_dependents();
+    if (lane == 0) {
+      mbar_arrive_expect_tx(sabar, (uint32_t)(kRows * lds));
+      tma_load_2d(smem_u32(base + A.smem_sfa), &A.tms, 0, row0, sabar);
+    }
+    for (int st = 0; st < nstages && ok; ++st) {
+      const int s = st % A.NS, round = st / A.NS;
+      if (round > 0 && !mbar_wait_bounded(empty0 + 8 * s, (uint32_t)((round - 1) & 1), A.err)) { ok = false; break; }
+      const uint32_t stage = smem_u32(base) + (uint32_t)s * kStageA;
+      if (lane == 0) {
+        mbar_arrive_expect_tx(full0 + 8 * s, (uint32_t)kStageA);
+        tma_load_2d(stage, &A.tm, st * kMxKC, row0, full0 + 8 * s);
+        tma_load_2d(stage + kStageA / 2, &A.tm, st * kMxKC, row0 + 64, full0 + 8 * s);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issue (lane 0) ----------------
+    if (lane == 0) {
+      const uint32_t bbase = smem_u32(base + A.smem_b);
+      for (int st = 0; st < nstages && ok; ++st) {
+        const int s = st % A.NS;
+        if (!mbar_wait_bounded(full0 + 8 * s, (uint32_t)((st / A.NS) & 1), A.err)) { ok = false; break; }
+        if (!mbar_wait_bounded(sfr0 + 8 * st, 0, A.err)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t astage = smem_u32(base) + (uint32_t)s * kStageA;
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const int kb = st * 4 + j;
+          const uint64_t adesc = smem_desc_sw128(astage + 32u * j);
+          const uint64_t bdesc = smem_desc_sw128(bbase + (uint32_t)(st * NBT * 128 + j * 32));
+          const uint32_t sel = (uint32_t)j << 30;
+          mma_mxf8(tmem + kMxColD + (uint32_t)((kb % NACC) * NBT), adesc, bdesc, idesc_mxf8(NBT, (uint32_t)j),
+                   (tmem + kMxColSFA + 4u * st) | sel, (tmem + kMxColSFB + 4u * st) | sel, kb >= NACC ? 1u : 0u);
+        }
+        tc_commit(empty0 + 8 * s);
+      }
+      tc_commit(dfull);
+    }
+    __syncwarp();
+  } else if (warp >= 8) {
+    // ---------------- scale writers (subpartition warp - 8), then the epilogue ----------------
+    const int sub = warp - 8;
+    const uint32_t tsub = tmem + ((uint32_t)(32 * sub) << 16);
+    // A scales, all chunks: lane l, column 4c + q = row l + 32q, bytes = the chunk's four 32-k scales
+    if (!mbar_wait_bounded(sabar, 0, A.err)) ok = false;
+    const uint8_t* sa = base + A.smem_sfa;
+    for (int c0 = 0; c0 < nstages && ok; c0 += 4) {
+      uint32_t v[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int c = c0 + (i >> 2), q = i & 3;
+        v[i] = c < nstages ? *reinterpret_cast<const uint32_t*>(sa + (lane + 32 * q) * lds + 4 * c) : 0u;
+      }
+      tc_st16(tsub + kMxColSFA + 4u * c0, v);
+    }
+    // B scales, slab by slab: column 4 st + n / 32 (lane n % 32), byte j = the slab's 32-k block
+    const uint8_t* sfb = base + A.smem_sfb;
+    for (int st = 0; st < nstages && ok; ++st) {
+      if (!mbar_wait_bounded(slab0 + 8 * st, 0, A.err)) { ok = false; break; }
+      uint32_t vb[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        vb[c] = 32 * c < NBT ? *reinterpret_cast<const uint32_t*>(sfb + st * 512 + lane * 16 + c * 4) : 0u;
+      asm volatile("tcgen05.st.sync.aligned.32x32b.x4.b32 [%0], {%1, %2, %3, %4};" ::"r"(tsub + kMxColSFB + 4u * st),
+                   "r"(vb[0]), "r"(vb[1]), "r"(vb[2]), "r"(vb[3])
+                   : "memory");
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(sfr0 + 8 * st);
+    }
+    if (ok && !mbar_wait_bounded(dfull, 0, A.err)) ok = false;
+    tc_fence_after();
+    if (ok) {
+      float d[NBT];
+#pragma unroll
+      for (int i = 0; i < NBT; ++i) d[i] = 0.f;
+#pragma unroll
+      for (int a = 0; a < NACC; ++a) {
+#pragma unroll
+        for (int c0 = 0; c0 < NBT; c0 += 16) {
+          uint32_t q[16];
+          tc_ld16(tsub + kMxColD + (uint32_t)(a * NBT + c0), q);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) d[c0 + i] += __uint_as_float(q[i]);
+        }
+      }
+      const int row = row0 + 32 * sub + lane;
+      if (row < A.N) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          float acc = 0.f;
+#pragma unroll
+          for (int t = kMxTerms - 1; t >= 0; --t) acc += d[t * MT + m];
+          store_out(A.out, A.out_dtype, (int64_t)m * A.out_stride + row, acc);
+        }
+      }
+    }
+    tc_fence_before();
+  } else {
+    // ---------------- activations -> e4m3 terms (warps 2..7), slab by slab ----------------
+    const int ptid = threadIdx.x - 64, pthreads = 192;
+    pdl_wait();
+    const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(base + A.smem_xraw);
+    if (ptid == 0) {
+      const uint32_t bytes = (uint32_t)A.K * 2u;
+      mbar_arrive_expect_tx(xbar, bytes * (uint32_t)MT);
+      for (int m = 0; m < MT; ++m)
+        bulk_g2s(smem_u32(base + A.smem_xraw) + m * bytes, A.x + (int64_t)m * A.x_stride, bytes, xbar);
+    }
+    if (!mbar_wait_bounded(xbar, 0, A.err)) ok = false;
+    uint8_t* bsm = base + A.smem_b;
+    uint8_t* sfb = base + A.smem_sfb;
+    for (int idx = ptid; idx < nstages * kBlkPerSlab; idx += pthreads) {
+      const int slab = idx / kBlkPerSlab, rem = idx - slab * kBlkPerSlab;
+      const int m = rem >> 2, jb = rem & 3, k0 = slab * kMxKC + jb * 32;
+      if (ok) {
+        float v[32];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const uint4 w = reinterpret_cast<const uint4*>(xr + (int64_t)m * A.K + k0)[q];
+          const uint32_t w4[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            v[8 * q + 2 * e] = bf16_bits_to_f32(w4[e] & 0xffffu);
+            v[8 * q + 2 * e + 1] = bf16_bits_to_f32(w4[e] >> 16);
+          }
+        }
+#pragma unroll
+        for (int t = 0; t < kMxTerms; ++t) {
+          float amax = 0.f;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(v[i]));
+          // S = 2^(e - 7) for amax in [2^e, 2^(e+1)): |r / S| < 256 <= 448; an all-zero block gets S = 2^-127
+          const int e = amax > 0.f ? (int)((__float_as_uint(amax) >> 23) & 0xff) - 127 : -120;
+          const int code = max(e - 7 + 127, 0);  // e8m0 byte of S
+          const float inv = code > 0 ? __uint_as_float((uint32_t)(254 - code) << 23) : 0.f;
+          const float sc = code > 0 ? __uint_as_float((uint32_t)code << 23) : 0.f;
+          uint32_t wd[8];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            const uint32_t p0 = f32x2_to_e4m3x2(v[4 * i] * inv, v[4 * i + 1] * inv);
+            const uint32_t p1 = f32x2_to_e4m3x2(v[4 * i + 2] * inv, v[4 * i + 3] * inv);
+            wd[i] = p0 | (p1 << 16);
+            const uint32_t h0 = e4m3x2_to_f16x2(p0), h1 = e4m3x2_to_f16x2(p1);
+            v[4 * i] = fmaf(-f16_bits_to_f32(h0 & 0xffffu), sc, v[4 * i]);
+            v[4 * i + 1] = fmaf(-f16_bits_to_f32(h0 >> 16), sc, v[4 * i + 1]);
+            v[4 * i + 2] = fmaf(-f16_bits_to_f32(h1 & 0xffffu), sc, v[4 * i + 2]);
+            v[4 * i + 3] = fmaf(-f16_bits_to_f32(h1 >> 16), sc, v[4 * i + 3]);
+          }
+          const int n = t * MT + m;
+          const uint32_t b0 = smem_u32(bsm) + b_offset_mx(NBT, n, k0);
+          const uint32_t b1 = smem_u32(bsm) + b_offset_mx(NBT, n, k0 + 16);
+          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(b0), "r"(wd[0]), "r"(wd[1]), "r"(wd[2]),
+                       "r"(wd[3])
+                       : "memory");
+          asm volatile("st.shared.v4.u32 [%0], {%1, %2, %3, %4};" ::"r"(b1), "r"(wd[4]), "r"(wd[5]), "r"(wd[6]),
+                       "r"(wd[7])
+                       : "memory");
+          sfb[slab * 512 + (n & 31) * 16 + (n >> 5) * 4 + jb] = (uint8_t)code;
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(slab0 + 8 * slab);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kTmemCols) : "memory");
+  }
+}
+
 }  // namespace tc
 }  // namespace fp4x

@@ -1,4 +1,4 @@
-"""GPU parity of the tcgen05 NVFP4 GEMV (shapes with M <= 8 tokens and at least 8,192 rows take the block-scaled
+"""GPU parity of the tcgen05 NVFP4 and MXFP8 GEMVs (shapes with M <= 8 tokens and at least 8,192 rows take the block-scaled
 tensor-core kernel; the others take the register-decode kernel, covered in test_gpu_gemv.py).
 
 The tensor-core kernel multiplies the stored e2m1 weights and e4m3 scales exactly and writes each activation as six
@@ -59,6 +59,50 @@ def test_nv4_tc_dynamic_range_and_zero_token(nv4_weights):
     x = x.to(torch.bfloat16)
     ref = (x.double().numpy() @ wdeq.T) * np.float64(np.float32(gs))
     y = F.nv4_linear(x.to(DEV), P.to(DEV), S.to(DEV), gs, out_dtype=torch.float32).cpu().numpy()
+    for r in (0, 1, 3):
+        assert rel_err(y[r], ref[r]) < 2e-4, r
+    assert np.all(y[2] == 0.0)
+
+
+# ----------------------------------------------------------------------------------------------------------
+# MXFP8 (kind::mxf8f6f4): e4m3 weights with e8m0 scales consumed as stored; activations as four e4m3 terms with
+# power-of-two scales per 32 elements (what they leave out is below 2^-15 of each block's largest element)
+# ----------------------------------------------------------------------------------------------------------
+
+@pytest.fixture(scope="module")
+def mx8_weights():
+    g = torch.Generator().manual_seed(41)
+    n = 16384 + 64
+    w = torch.randn(n, K, generator=g) * 0.02
+    codes, sc = F.quantize_mx8(w)
+    return codes, sc, O.mx8_dequant(codes.view(torch.uint8).numpy(), sc.numpy()).astype(np.float64)
+
+
+@pytest.mark.parametrize("m", [1, 3, 8])
+def test_mx8_tc_matches_oracle(mx8_weights, m):
+    codes, sc, wdeq = mx8_weights
+    g = torch.Generator().manual_seed(200 + m)
+    x = torch.randn(m, K, generator=g).to(torch.bfloat16)
+    ref = x.double().numpy() @ wdeq.T
+    cd, sd, xd = codes.to(DEV), sc.to(DEV), x.to(DEV)
+    y32 = F.mx8_linear(xd, cd, sd, None, out_dtype=torch.float32).cpu()
+    assert rel_err(y32, ref) < 2e-4
+    y16 = F.mx8_linear(xd, cd, sd, None).float().cpu()
+    assert rel_err(y16, ref) < 1e-2
+    assert torch.equal(F.mx8_linear(xd, cd, sd, None, out_dtype=torch.float32).cpu(), y32)
+
+
+def test_mx8_tc_dynamic_range_and_zero_token(mx8_weights):
+    codes, sc, wdeq = mx8_weights
+    g = torch.Generator().manual_seed(9)
+    x = torch.randn(4, K, generator=g) * 1e-2
+    x[0, ::97] = 3000.0
+    x[1] *= 1e-8
+    x[2] = 0.0
+    x[3, :32] = 0.0
+    x = x.to(torch.bfloat16)
+    ref = x.double().numpy() @ wdeq.T
+    y = F.mx8_linear(x.to(DEV), codes.to(DEV), sc.to(DEV), None, out_dtype=torch.float32).cpu().numpy()
     for r in (0, 1, 3):
         assert rel_err(y[r], ref[r]) < 2e-4, r
     assert np.all(y[2] == 0.0)
