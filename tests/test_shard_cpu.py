@@ -1,0 +1,106 @@
+"""Host logic of the vocab-sharded head (fp4x_shard.py) on CPU: shard ranges, candidate packing, and the
+candidate exchange over a world-size-2 gloo process group; plus the exactness argument of the merge, checked with
+the oracle (the global top-C equals the top-C of the union of the shard top-Cs)."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from fp4x_shard import gather_candidates, pack_candidates, shard_range, unpack_candidates
+from oracle import fp4x_oracle as O
+
+
+def test_shard_range_covers_vocab():
+    for V, world in ((248320, 1), (248320, 2), (248320, 8), (65536, 4), (1000, 3)):
+        spans = [shard_range(V, r, world) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == V
+        assert all(spans[i][1] == spans[i + 1][0] for i in range(world - 1))
+    with pytest.raises(ValueError):
+        shard_range(100, 2, 2)
+    with pytest.raises(ValueError):
+        shard_range(1, 0, 2)
+
+
+def test_pack_unpack_roundtrip():
+    g = torch.Generator().manual_seed(3)
+    m, c = 3, 512
+    co = torch.randn(m, c, generator=g)
+    ex = torch.randn(m, c, generator=g)
+    gi = torch.randint(0, 248320, (m, c), generator=g, dtype=torch.int32)
+    packed = pack_candidates(co, ex, gi)
+    assert packed.shape == (3, m, c) and packed.dtype == torch.float32
+    # two ranks' packs laid end to end, as the all-gather produces them
+    both = torch.cat([packed.reshape(-1), packed.reshape(-1) * 0 + packed.reshape(-1)])
+    a, b, ids = unpack_candidates(both, 2, m, c)
+    assert torch.equal(a[0], co) and torch.equal(b[1], ex) and torch.equal(ids[0], gi) and torch.equal(ids[1], gi)
+    with pytest.raises(TypeError):
+        pack_candidates(co, ex, gi.long())
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _exchange_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        m, c = 3, 64
+        g = torch.Generator().manual_seed(100 + rank)
+        co = torch.randn(m, c, generator=g)
+        ex = torch.randn(m, c, generator=g)
+        gi = torch.randint(rank * 1000, rank * 1000 + 1000, (m, c), generator=g, dtype=torch.int32)
+        a, b, ids = gather_candidates(co, ex, gi)
+        ok = True
+        for r in range(world):
+            g2 = torch.Generator().manual_seed(100 + r)
+            ok &= torch.equal(a[r], torch.randn(m, c, generator=g2))
+            ok &= torch.equal(b[r], torch.randn(m, c, generator=g2))
+            ok &= torch.equal(ids[r], torch.randint(r * 1000, r * 1000 + 1000, (m, c), generator=g2,
+                                                    dtype=torch.int32))
+        q.put((rank, bool(ok)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_candidates_two_ranks_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_exchange_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert results == {0: True, 1: True}
+
+
+def test_sharded_topc_union_contains_global_topc():
+    """The merge step's exactness: the global top-C (value desc, id asc) is the top-C of the union of per-shard
+    top-Cs, for any split, ties included."""
+    rng = np.random.default_rng(5)
+    V, m, C = 4096, 3, 64
+    vals = rng.standard_normal((m, V)).astype(np.float32)
+    vals[:, 100:140] = vals[:, 50:51]  # a block of exact ties
+    ref = O.topk_order(vals, C)
+    for parts in (2, 4, 8):
+        per = V // parts
+        cand_v, cand_i = [], []
+        for p in range(parts):
+            local = O.topk_order(vals[:, p * per:(p + 1) * per], C) + p * per
+            cand_i.append(local)
+            cand_v.append(np.take_along_axis(vals, local, axis=1))
+        ci = np.concatenate(cand_i, axis=1)
+        cv = np.concatenate(cand_v, axis=1)
+        for r in range(m):
+            order = np.lexsort((ci[r], -cv[r].astype(np.float64)))[:C]
+            assert np.array_equal(np.sort(ci[r][order]), np.sort(ref[r]))
