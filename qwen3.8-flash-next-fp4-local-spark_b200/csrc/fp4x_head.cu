@@ -57,9 +57,37 @@ __global__ void __launch_bounds__(512) topk_hist_kernel(const float* vals, int64
 
 // block-wide: the histogram bin (scanned from the top) that contains rank `need` (1-based); also returns the count
 // strictly above that bin.  `h` is in shared memory, nb bins; all threads get the result.
+// Exclusive prefix sum of one value per thread over the block (blockDim.x a multiple of 32, at most 1024), in
+// thread order; wtot is shared scratch of 32 ints.  Every thread of the block must call it.
+FP4X_DEV int block_exclusive_scan(int v, int* wtot) {
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int y = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += y;
+  }
+  if (lane == 31) wtot[w] = incl;
+  __syncthreads();
+  if (w == 0) {
+    const int t = lane < nw ? wtot[lane] : 0;
+    int ti = t;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, ti, o);
+      if (lane >= o) ti += y;
+    }
+    wtot[lane] = ti - t;
+  }
+  __syncthreads();
+  const int res = wtot[w] + incl - v;
+  __syncthreads();
+  return res;
+}
+
 template <int NT>
 FP4X_DEV void find_rank_bin(const int* h, int nb, int need, int& bin_out, int& above_out, int* scratch) {
-  // scratch: NT ints + 2
+  // scratch: NT + 34 ints
   const int per = (nb + NT - 1) / NT;
   const int t = threadIdx.x;
   // thread t owns bins counted from the top: top index = nb-1 - (t*per + j)
@@ -68,25 +96,7 @@ FP4X_DEV void find_rank_bin(const int* h, int nb, int need, int& bin_out, int& a
     const int bi = nb - 1 - (t * per + j);
     if (bi >= 0) tot += h[bi];
   }
-  scratch[t] = tot;
-  __syncthreads();
-  // serial-in-warp exclusive scan over NT thread totals (NT <= 1024): warp 0 does it
-  if (t < 32) {
-    int run = 0;
-    for (int base = 0; base < NT; base += 32) {
-      int v = scratch[base + t];
-      int incl = v;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, incl, o);
-        if (t >= o) incl += y;
-      }
-      scratch[base + t] = run + incl - v;  // exclusive
-      run += __shfl_sync(0xffffffffu, incl, 31);
-    }
-  }
-  __syncthreads();
-  const int before = scratch[t];
+  const int before = block_exclusive_scan(tot, scratch + NT + 2);
   if (before < need && before + tot >= need) {
     int cum = before;
     for (int j = 0; j < per; ++j) {
@@ -112,7 +122,7 @@ FP4X_DEV void find_rank_bin(const int* h, int nb, int need, int& bin_out, int& a
 __global__ void __launch_bounds__(512) topk_filter_kernel(const float* vals, int64_t ld, int V, int C,
                                                           const int* hist, int* cnt, uint64_t* cand) {
   __shared__ int h[kHistBins];
-  __shared__ int scr[512 + 2];
+  __shared__ int scr[512 + 34];
   const int m = blockIdx.y;
   pdl_wait();
   for (int i = threadIdx.x; i < kHistBins; i += blockDim.x) h[i] = hist[(int64_t)m * kHistBins + i];
@@ -154,8 +164,9 @@ struct SelectShared {
   uint32_t sel[kMaxVocab / 32];   // selected indices
   uint32_t eq[kMaxVocab / 32];    // candidates whose key equals the final prefix
   int h[kHistBins];
-  int scr[kSelThreads + 2];
+  int scr[kSelThreads + 34];
   int wpre[kSelThreads + 1];
+  int wtot[32];
 };
 // the candidate list (uint64) follows SelectShared in dynamic shared memory at a 16-byte aligned offset
 constexpr size_t kListOffset = (sizeof(SelectShared) + 15) / 16 * 16;
@@ -233,18 +244,7 @@ FP4X_DEV void select_top(const Src& src, int C, int V, SelectShared& S) {
     const int w0 = threadIdx.x * per;
     int cnt = 0;
     for (int w = w0; w < min(nw, w0 + per); ++w) cnt += __popc(S.eq[w]);
-    S.wpre[threadIdx.x] = cnt;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int run = 0;
-      for (int t = 0; t < (int)blockDim.x; ++t) {
-        const int c = S.wpre[t];
-        S.wpre[t] = run;
-        run += c;
-      }
-    }
-    __syncthreads();
-    int before = S.wpre[threadIdx.x];
+    int before = block_exclusive_scan(cnt, S.wtot);
     for (int w = w0; w < min(nw, w0 + per) && before < need; ++w) {
       uint32_t bitsw = S.eq[w];
       while (bitsw && before < need) {
@@ -265,19 +265,7 @@ FP4X_DEV void emit_selected(const SelectShared& S, int V, int C, int32_t* idx_ou
   const int w0 = threadIdx.x * per;
   int cnt = 0;
   for (int w = w0; w < min(nw, w0 + per); ++w) cnt += __popc(S.sel[w]);
-  int* wpre = const_cast<int*>(S.wpre);
-  wpre[threadIdx.x] = cnt;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0;
-    for (int t = 0; t < (int)blockDim.x; ++t) {
-      const int c = wpre[t];
-      wpre[t] = run;
-      run += c;
-    }
-  }
-  __syncthreads();
-  int pos = wpre[threadIdx.x];
+  int pos = block_exclusive_scan(cnt, const_cast<int*>(S.wtot));
   for (int w = w0; w < min(nw, w0 + per); ++w) {
     uint32_t b = S.sel[w];
     while (b) {
@@ -487,16 +475,7 @@ __global__ void __launch_bounds__(kSelThreads) head_merge_kernel(const float* co
   const int w0 = threadIdx.x * per;
   int cnt = 0;
   for (int w = w0; w < min(nw, w0 + per); ++w) cnt += __popc(S.sel[w]);
-  S.wpre[threadIdx.x] = cnt;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    int run = 0;
-    for (int t = 0; t < (int)blockDim.x; ++t) {
-      const int c = S.wpre[t];
-      S.wpre[t] = run;
-      run += c;
-    }
-  }
+  S.wpre[threadIdx.x] = block_exclusive_scan(cnt, S.wtot);
   __syncthreads();
   for (int i = threadIdx.x; i < P * C; i += blockDim.x) {
     const int p = i / C, c = i - p * C;
