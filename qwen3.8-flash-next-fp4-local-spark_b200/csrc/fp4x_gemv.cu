@@ -9,6 +9,7 @@
 
 #include "fp4x_gemv.cuh"
 #include "fp4x_tc.cuh"
+#include "fp4x_tc_int2.cuh"
 #include "fp4x_host.h"
 
 namespace fp4x {
@@ -142,6 +143,22 @@ static int encode_scale_box(CUtensorMap* tm, const void* ptr, int64_t rows, int6
                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) return fail(FP4X_ERR_UNSUPPORTED, "scale tensor map encode failed (" + std::to_string((int)r) + ")");
+  return FP4X_OK;
+}
+
+// [rows][row_bytes] u8, box {box_bytes, box_rows}, 64-byte swizzle when box_bytes is 64 (the INT2 code tiles)
+static int encode_box(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t row_bytes, int box_bytes, int box_rows) {
+  EncodeTiledFn enc = encode_fn();
+  if (!enc) return fail(FP4X_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
+  const cuuint64_t gdim[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
+  const cuuint64_t gstride[1] = {(cuuint64_t)row_bytes};
+  const cuuint32_t box[2] = {(cuuint32_t)box_bytes, (cuuint32_t)box_rows};
+  const cuuint32_t es[2] = {1, 1};
+  const CUtensorMapSwizzle sw = box_bytes == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_NONE;
+  CUresult r = enc(tm, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), gdim, gstride, box, es,
+                   CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(FP4X_ERR_UNSUPPORTED, "tensor map encode failed (" + std::to_string((int)r) + ")");
   return FP4X_OK;
 }
 
@@ -582,6 +599,48 @@ static int run_mx8_tc(const void* x, int64_t x_stride, const void* w, const void
   }
 }
 
+// INT2 head logits on tcgen05 (fp4x_tc_int2.cuh): M <= 16 tokens, at least 32 row tiles of 128, groups of 16 or
+// 32, K a multiple of 256 with the B operand (K x 32 bytes) fitting beside the stages.  Returns 1 when the shape is
+// not covered (the caller then uses the register-decode kernel).
+static int run_int2_tc(const void* x, int64_t x_stride, const void* p, const void* s, int group, void* out,
+                       void* out_bf16, int64_t out_stride, int out_dtype, int64_t m, int64_t n, int64_t k,
+                       void* stream) {
+  const DeviceFacts& dv = device_facts();
+  if (m < 1 || m > tc::kI2MaxM || (group != 16 && group != 32) || k % tc::kI2KC != 0 || n < 32 * tc::kRows ||
+      n > (1 << 30))
+    return 1;
+  if (!aligned(x, 16) || x_stride % 8 != 0 || x_stride < k || !aligned(p, 16) || !aligned(s, 16) || !out ||
+      out_stride < n)
+    return 1;
+  int rc;
+  if ((rc = check_out_dtype(out_dtype))) return rc;
+  const int b_bytes = (int)(k / 64) * 2048;
+  const int misc = 1024;
+  const int fixed = b_bytes + misc + 1024;
+  int ns = (dv.smem_optin - fixed) / tc::kI2StageBytes;
+  if (ns > tc::kI2MaxStages) ns = tc::kI2MaxStages;
+  if (ns < 4) return 1;
+  tc::I2Args a;
+  std::memset(&a, 0, sizeof(a));
+  a.NS = ns;
+  a.smem_b = ns * tc::kI2StageBytes;  // multiple of 1024
+  a.smem_misc = a.smem_b + b_bytes;
+  const int smem_total = a.smem_misc + misc + 1024;
+  if ((rc = encode_box(&a.tm, p, n, k / 4, 64, tc::kRows))) return rc;
+  if ((rc = encode_box(&a.tms, s, n, 2 * k / group, 512 / group, tc::kRows))) return rc;
+  a.x = (const __nv_bfloat16*)x; a.x_stride = x_stride;
+  a.out = out; a.out_bf16 = out_bf16; a.out_stride = out_stride; a.out_dtype = out_dtype;
+  a.M = (int)m; a.N = (int)n; a.K = (int)k; a.group = group;
+  a.tiles = (int)((n + tc::kRows - 1) / tc::kRows);
+  a.err = dev_error_ptr();
+  const unsigned grid = (unsigned)std::min(a.tiles, dv.sms);
+  auto kern = tc::int2_tc_kernel;
+  cudaError_t e = ensure_smem_attr((const void*)kern, smem_total);
+  if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
+  return check_launch(launch_pdl(kern, dim3(grid), dim3(tc::kI2Threads), (size_t)smem_total, (cudaStream_t)stream, a),
+                      "int2 tcgen05 launch");
+}
+
 // shared path of the single-matrix GEMVs
 static int run_gemv(int fmt, const void* x, int64_t x_stride, const void* p0, const void* p1, const void* sc,
                     float post, int group, void* out, void* out2, int64_t out_stride, int out_dtype, int64_t m,
@@ -758,6 +817,8 @@ int fp4x_w6_linear(const void* x, int64_t x_stride, const void* lo, const void* 
 int fp4x_int2_logits(const void* x, int64_t x_stride, const void* p, const void* s, int group, void* out,
                      int64_t out_stride, int out_dtype, void* out_bf16, int64_t m, int64_t n, int64_t k, void* ws,
                      size_t ws_bytes, int32_t* counters, int64_t n_counters, void* stream) {
+  const int rc = run_int2_tc(x, x_stride, p, s, group, out, out_bf16, out_stride, out_dtype, m, n, k, stream);
+  if (rc <= 0) return rc;
   return run_gemv(FMT_INT2, x, x_stride, p, nullptr, s, 1.f, group, out, out_bf16, out_stride, out_dtype, m, n, k,
                   ws, ws_bytes, counters, n_counters, stream, EPI_HEAD);
 }

@@ -106,3 +106,57 @@ def test_mx8_tc_dynamic_range_and_zero_token(mx8_weights):
     for r in (0, 1, 3):
         assert rel_err(y[r], ref[r]) < 2e-4, r
     assert np.all(y[2] == 0.0)
+
+
+# ----------------------------------------------------------------------------------------------------------
+# INT2 head logits (kind::f16, A operand decoded into tensor memory): the decoded weights are the reference's
+# bf16((code - 1.5) * s) exactly, so the only difference from the oracle's exact sums is fp32 accumulation
+# (the bound of the register-decode kernel's test, 5e-5 of max |ref|, applies unchanged).
+# ----------------------------------------------------------------------------------------------------------
+
+@pytest.fixture(scope="module")
+def int2_weights():
+    g = torch.Generator().manual_seed(51)
+    n = 16384 + 64  # a partial last tile
+    w = torch.randn(n, K, generator=g) * 0.02
+    P, S = F.quantize_int2(w, group=16)
+    return P, S
+
+
+@pytest.mark.parametrize("m", [1, 3, 8, 16])
+def test_int2_tc_matches_oracle(int2_weights, m):
+    P, S = int2_weights
+    n = P.shape[0]
+    g = torch.Generator().manual_seed(300 + m)
+    x = torch.randn(m, K, generator=g).to(torch.bfloat16)
+    ref = O.int2_logits(x.float().numpy(), P.numpy(), S.numpy())
+    Pd, Sd, xd = P.to(DEV), S.to(DEV), x.to(DEV)
+    ob = torch.empty((m, n), dtype=torch.bfloat16, device=DEV)
+    out = F.int2_logits(xd, Pd, Sd, n, out_bf16=ob)
+    assert rel_err(out.cpu(), ref) < 5e-5
+    assert torch.equal(ob, out.to(torch.bfloat16))
+    assert torch.equal(F.int2_logits(xd, Pd, Sd, n), out)  # deterministic
+
+
+def test_int2_tc_rows_independent_of_tile_position(int2_weights):
+    """A row's logit does not depend on where its 128-row tile starts: a vocabulary shard that starts mid-tile gives
+    the same bits as the whole head (what the sharded head's merge relies on)."""
+    P, S = int2_weights
+    x = torch.randn(3, K, generator=torch.Generator().manual_seed(77)).to(torch.bfloat16).to(DEV)
+    Pd, Sd = P.to(DEV), S.to(DEV)
+    n = P.shape[0]
+    full = F.int2_logits(x, Pd, Sd, n)
+    part = F.int2_logits(x, Pd[64:], Sd[64:], n - 64)
+    assert torch.equal(part, full[:, 64:])
+
+
+@pytest.mark.parametrize("grp,k", [(32, 2560), (16, 4096), (32, 4096)])
+def test_int2_tc_groups_and_depths(grp, k):
+    g = torch.Generator().manual_seed(61 + k + grp)
+    n = 8192
+    w = torch.randn(n, k, generator=g) * 0.02
+    P, S = F.quantize_int2(w, group=grp)
+    x = torch.randn(3, k, generator=g).to(torch.bfloat16)
+    ref = O.int2_logits(x.float().numpy(), P.numpy(), S.numpy())
+    out = F.int2_logits(x.to(DEV), P.to(DEV), S.to(DEV), n)
+    assert rel_err(out.cpu(), ref) < 5e-5
