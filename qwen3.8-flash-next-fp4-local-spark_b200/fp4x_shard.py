@@ -9,6 +9,10 @@ ascending) and the argmax of the exact values among them.
 
 This is exact: the global top-C is a subset of the union of the per-shard top-Cs, and the coarse value of a row
 does not depend on how the vocabulary is split (the INT2 kernel sums each row in an order fixed by K alone).
+
+`ShardedFastHead.full` also returns the whole [M, V] bf16 logit vector the single-GPU head returns (coarse values,
+with the exact values of the selected rows scattered in, `x/fp4patch.py:378`): one more all-gather of the shards'
+bf16 logits, after which the rows a shard rescored but the merge did not select get their coarse value back.
 """
 from __future__ import annotations
 
@@ -56,6 +60,37 @@ def gather_candidates(coarse, exact, gidx, group=None):
     return unpack_candidates(out, world, m, c)
 
 
+def gather_full(full_local, V, rank, world, group=None):
+    """All-gather every rank's bf16 logits [M, rows_r] into [M, V] (shards in rank order; the last shard, which may
+    be longer, sets the padded width of the collective)."""
+    m, rows = full_local.shape
+    start, stop = shard_range(V, rank, world)
+    if rows != stop - start:
+        raise ValueError(f"rank {rank} holds {rows} logits, expected {stop - start}")
+    width = V - shard_range(V, world - 1, world)[0]
+    buf = full_local
+    if rows != width:
+        buf = torch.zeros((m, width), dtype=full_local.dtype, device=full_local.device)
+        buf[:, :rows] = full_local
+    out = torch.empty((world * m, width), dtype=full_local.dtype, device=full_local.device)
+    dist.all_gather_into_tensor(out, buf.contiguous(), group=group)
+    out = out.view(world, m, width)
+    full = torch.empty((m, V), dtype=full_local.dtype, device=full_local.device)
+    for r in range(world):
+        a, b = shard_range(V, r, world)
+        full[:, a:b] = out[r, :, :b - a]
+    return full
+
+
+def fix_full(full, co, gi, idx, exact):
+    """In place: the rows every shard rescored get their coarse value back (bf16 of the fp32 coarse logit), then the
+    merged selection gets its exact values.  co, gi: [P, M, C] gathered candidates; idx, exact: [M, C] merged."""
+    p, m, c = co.shape
+    full.scatter_(1, gi.permute(1, 0, 2).reshape(m, p * c).long(), co.permute(1, 0, 2).reshape(m, p * c).to(full.dtype))
+    full.scatter_(1, idx.long(), exact.to(full.dtype))
+    return full
+
+
 class ShardedFastHead:
     """This rank's shard of the fast target head.
 
@@ -71,7 +106,7 @@ class ShardedFastHead:
         if rows < C:
             raise ValueError(f"shard of {rows} rows is smaller than C={C}")
         self.P, self.S, self.w8, self.s8 = F._rows(P), F._rows(S), F._rows(F._u8(w8)), F._rows(F._u8(s8))
-        self.V, self.C, self.world, self.group = V, C, world, group
+        self.V, self.C, self.rank, self.world, self.group = V, C, rank, world, group
 
     def local(self, h):
         """The shard's own candidates: (coarse, exact, global ids) [M, C] each, and the coarse bf16 logits."""
@@ -96,3 +131,17 @@ class ShardedFastHead:
         else:
             co, ex, gi = gather_candidates(coarse, exact, gidx, self.group)
         return F.head_merge(co, ex, gi, self.V)
+
+    def full(self, h):
+        """The single-GPU head's outputs on every rank: (full bf16 [M, V], idx int32 [M, C], exact fp32 [M, C],
+        argmax int32 [M]) -- `F.fast_head`'s return, bit for bit."""
+        coarse, exact, gidx, full_local = self.local(h)
+        if self.world == 1:
+            co, ex, gi = coarse[None], exact[None], gidx[None]
+        else:
+            co, ex, gi = gather_candidates(coarse, exact, gidx, self.group)
+        idx, _, exm, amax = F.head_merge(co, ex, gi, self.V)
+        if self.world == 1:
+            return full_local, idx, exm, amax
+        full = gather_full(full_local, self.V, self.rank, self.world, self.group)
+        return fix_full(full, co, gi, idx, exm), idx, exm, amax

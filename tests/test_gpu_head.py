@@ -209,3 +209,17 @@ def test_sharded_head_merge_equals_unsharded(parts):
     assert torch.equal(idx, idx_full)
     assert torch.equal(amax, amax_full)
     assert torch.equal(exm, exact_full)
+
+
+def test_sharded_head_single_rank_full_equals_fast_head():
+    """world = 1: ShardedFastHead.full is F.fast_head (no collective)."""
+    from fp4x_shard import ShardedFastHead
+    V, K, C, m = 20000, 2560, 512, 3
+    w = gen(16, V, K, std=0.02).to(DEV)
+    codes, sc = F.quantize_mx8(w)
+    P, S = F.quantize_int2(F.mx8_dequant(codes, sc), group=16)
+    h = gen(17, m, K).to(torch.bfloat16).to(DEV)
+    ref = F.fast_head(h, P, S, codes, sc, C)
+    got = ShardedFastHead(P, S, codes, sc, V, 0, 1, C=C).full(h)
+    for a, b in zip(got, ref):
+        assert torch.equal(a, b)

@@ -1,5 +1,5 @@
 """Vocab-sharded fast head over two GPUs (one process per GPU, NCCL all-gather): the merged candidates and argmax
-equal the unsharded head's.  Skipped unless two GPUs are visible."""
+equal the unsharded head's, and so does the full [M, V] bf16 logit vector.  Skipped unless two GPUs are visible."""
 import os
 import socket
 
@@ -47,9 +47,12 @@ def _worker(rank, world, port, q):
         a, b = shard_range(V, rank, world)
         head = ShardedFastHead(P[a:b], S[a:b], codes[a:b], sc[a:b], V, rank, world, C=C)
         idx, _, exact, amax = head(h)
-        _, idx_full, exact_full, amax_full = F.fast_head(h, P, S, codes, sc, C)
+        full_ref, idx_full, exact_full, amax_full = F.fast_head(h, P, S, codes, sc, C)
+        full, idx2, exact2, amax2 = head.full(h)
         torch.cuda.synchronize()
         ok = torch.equal(idx, idx_full) and torch.equal(amax, amax_full) and torch.equal(exact, exact_full)
+        ok = ok and torch.equal(full, full_ref) and torch.equal(idx2, idx_full) and torch.equal(amax2, amax_full)
+        ok = ok and torch.equal(exact2, exact_full)
         q.put((rank, bool(ok)))
     finally:
         dist.destroy_process_group()

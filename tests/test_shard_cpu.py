@@ -10,7 +10,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from fp4x_shard import gather_candidates, pack_candidates, shard_range, unpack_candidates
+from fp4x_shard import fix_full, gather_candidates, gather_full, pack_candidates, shard_range, unpack_candidates
 from oracle import fp4x_oracle as O
 
 
@@ -104,3 +104,52 @@ def test_sharded_topc_union_contains_global_topc():
         for r in range(m):
             order = np.lexsort((ci[r], -cv[r].astype(np.float64)))[:C]
             assert np.array_equal(np.sort(ci[r][order]), np.sort(ref[r]))
+
+
+def _full_worker(rank, world, port, q):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        V, m = 1001, 3  # 3 ranks: shards of 333, 333, 335 (the last one is longer)
+        ref = (torch.arange(m * V, dtype=torch.float32).reshape(m, V) * 0.25).to(torch.bfloat16)
+        a, b = shard_range(V, rank, world)
+        full = gather_full(ref[:, a:b].clone(), V, rank, world)
+        q.put((rank, bool(torch.equal(full, ref))))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_gather_full_unequal_shards_gloo():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_full_worker, args=(r, 3, port, q)) for r in range(3)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert results == {0: True, 1: True, 2: True}
+
+
+def test_fix_full_restores_unselected_candidates():
+    """After the all-gather every shard's rescored rows carry exact values; only the merged selection may keep them."""
+    g = torch.Generator().manual_seed(9)
+    P_, m, V, C = 2, 3, 400, 8
+    coarse = torch.randn(m, V, generator=g)
+    exact = coarse + 0.01 * torch.randn(m, V, generator=g)
+    per = V // P_
+    gi = torch.stack([torch.stack([torch.randperm(per, generator=g)[:C] + p * per for _ in range(m)])
+                      for p in range(P_)]).to(torch.int32)                      # [P, M, C] shard candidates
+    co = torch.gather(coarse[None].expand(P_, m, V), 2, gi.long())
+    full = coarse.to(torch.bfloat16)
+    for p in range(P_):                                                         # what each shard's head wrote
+        full.scatter_(1, gi[p].long(), torch.gather(exact, 1, gi[p].long()).to(torch.bfloat16))
+    idx = torch.sort(gi.permute(1, 0, 2).reshape(m, P_ * C)[:, ::2], dim=1).values[:, :C]  # a merged selection
+    exm = torch.gather(exact, 1, idx.long())
+    fix_full(full, co, gi, idx, exm)
+    want = coarse.to(torch.bfloat16)
+    want.scatter_(1, idx.long(), exm.to(torch.bfloat16))
+    assert torch.equal(full, want)
