@@ -473,30 +473,41 @@ FP4X_DEV uint32_t w6_lane(uint32_t lo_src, uint32_t hi_src) {
   return (lo_src & 0x000F000Fu) | (hi_src & 0x00300030u) | 0x64006400u;
 }
 
-// W6: a chunk of the low-nibble plane is one 32-group G (thread: 8 k = 32G + 8tq + r); steps 2G + h
+// W6: a chunk of the low-nibble plane is one 32-group G (thread: 8 k = 32G + 8tq + r); steps 2G + h.
+// W6 stages always use 128-byte low-nibble boxes; NCHK 8 is the two-box stage (512 k: 128-byte high-bit rows,
+// 32 scale bytes per row), NCHK 4 the one-box stage (256 k: 64-byte high-bit rows, 16 scale bytes).  Every
+// address of the stage is a per-thread base XOR a constant: the bases have the varying bits clear (1024-aligned
+// planes, whole rows), and the varying parts (chunk pair, group) sit in bits the thread's fixed parts leave free.
 template <int NT, int NCHK>
 FP4X_DEV void stage_w6(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) {
+  constexpr int BI1 = NCHK == 8 ? 128 : 64;
+  constexpr int SB = NCHK == 8 ? 32 : 16;
   const uint32_t kNeg1056 = 0xE420E420u;
-  const int G0 = b * c.CPB + c0;
+  const int G0 = b * 8 + c0;
+  const uint32_t a0 = c.p0 + (uint32_t)b * (uint32_t)(kRB * 128) + c.lrow0 + 16u * (uint32_t)((c0 + c.lsel) ^ c.lswz);
+  uint32_t hb[2], sb[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int row = c.rbase + c.g + 8 * q;
+    hb[q] = c.p1 + swz((uint32_t)(row * BI1 + 8 * G0 + 2 * c.tq), BI1);
+    sb[q] = c.sc + (uint32_t)(row * SB + 2 * G0);
+  }
   uint32_t r[NCHK / 2][4];
   uint32_t hs[NCHK][2];
   uint32_t b0[2 * NCHK][NT], b1[2 * NCHK][NT];
   uint32_t sw[2][NCHK / 2];
 #pragma unroll
-  for (int u = 0; u < NCHK / 2; ++u) ld_pair(c, b, c0 + 2 * u, r[u][0], r[u][1], r[u][2], r[u][3]);
+  for (int u = 0; u < NCHK / 2; ++u) ldsm_x4(a0 ^ (32u * u), r[u][0], r[u][1], r[u][2], r[u][3]);
 #pragma unroll
   for (int gg = 0; gg < NCHK; ++gg)
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {
-      const int row = c.rbase + c.g + 8 * q;
-      hs[gg][q] = lds16(c.p1 + swz((uint32_t)(row * c.BI1 + 8 * (G0 + gg) + 2 * c.tq), c.BI1));
-    }
+    for (int q = 0; q < 2; ++q) hs[gg][q] = lds16(hb[q] ^ (8u * gg));
 #pragma unroll
   for (int s = 0; s < 2 * NCHK; ++s) load_b<NT>(c, 2 * G0 + s, b0[s], b1[s]);
 #pragma unroll
   for (int i = 0; i < NCHK / 2; ++i) {
-    sw[0][i] = lds32(c.sc + (c.rbase + c.g) * c.SB + 2 * G0 + 4 * i);
-    sw[1][i] = lds32(c.sc + (c.rbase + c.g + 8) * c.SB + 2 * G0 + 4 * i);
+    sw[0][i] = lds32(sb[0] + 4 * i);
+    sw[1][i] = lds32(sb[1] + 4 * i);
   }
 #pragma unroll
   for (int gg = 0; gg < NCHK; ++gg) {
