@@ -402,7 +402,8 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
 // ------------------------------------------------------------------------------------------------------
 template <int FMT, int NT, int EPI, int SHAPE>
 static int launch_s(const Plan& pl, const GemvArgs& a, int64_t batch, cudaStream_t st) {
-  auto kern = gemv_kernel<FMT, NT, EPI, SHAPE>;
+  const bool wide = (int64_t)pl.CPP * pl.KP * batch <= device_facts().sms;
+  auto kern = wide ? gemv_kernel_wide<FMT, NT, EPI, SHAPE> : gemv_kernel<FMT, NT, EPI, SHAPE>;
   cudaError_t e = ensure_smem_attr((const void*)kern, pl.smem_total);
   if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
   if (pl.cluster > 1) {

@@ -782,7 +782,7 @@ FP4X_DEV void run_epilogue(const GemvArgs& A, const GemvItem& it, int row0, cons
 // the kernel
 // ------------------------------------------------------------------------------------------------------
 template <int FMT, int NT, int EPI, int SHAPE>
-__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvArgs A) {
+FP4X_DEV void gemv_body(const GemvArgs& A) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   // stages need 1024-byte alignment for the swizzled TMA tiles; the host adds 1 KB of slack
   uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -1065,6 +1065,18 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
     if (++chunk == A.NCH) { chunk = 0; ++blk; }
   }
   if (ok && cur >= 0) flush(cur);
+}
+
+// Two entry points with one body.  Plans with more CTAs than SMs keep two CTAs per SM (at most ~100 registers per
+// thread); plans with at most one CTA per SM take the wide entry, whose 128-register budget buys the decode loops
+// more instruction-level parallelism and still leaves room on the SM for one CTA of the next kernel in the chain.
+template <int FMT, int NT, int EPI, int SHAPE>
+__global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant__ GemvArgs A) {
+  gemv_body<FMT, NT, EPI, SHAPE>(A);
+}
+template <int FMT, int NT, int EPI, int SHAPE>
+__global__ void __maxnreg__(128) gemv_kernel_wide(const __grid_constant__ GemvArgs A) {
+  gemv_body<FMT, NT, EPI, SHAPE>(A);
 }
 
 }  // namespace fp4x
