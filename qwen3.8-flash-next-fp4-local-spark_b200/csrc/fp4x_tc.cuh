@@ -133,9 +133,28 @@ FP4X_DEV uint32_t e4m3_code_ceil(float v) {
   return c;
 }
 
+// packed fp32 pairs (sm_100 f32x2 arithmetic: each lane rounds exactly as the scalar instruction)
+FP4X_DEV void mul2(float& d0, float& d1, float a0, float a1, float b) {
+  uint64_t a, bb, d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(bb) : "f"(b));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(bb));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(d0), "=f"(d1) : "l"(d));
+}
+// (c0, c1) += (a0, a1) * b
+FP4X_DEV void fma2(float& c0, float& c1, float a0, float a1, float b) {
+  uint64_t a, bb, c;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(a0), "f"(a1));
+  asm("mov.b64 %0, {%1, %1};" : "=l"(bb) : "f"(b));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(c) : "f"(c0), "f"(c1));
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(c) : "l"(a), "l"(bb));
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(c0), "=f"(c1) : "l"(c));
+}
+
 // One 16-element block of a token: the kTerms e2m1 terms (8 bytes each) and their scale codes.  v holds the
 // unscaled residual r; term t quantizes 4^t r (the factor keeps the scales inside e4m3's range) and removes
-// q S / 4^t from r.  The reciprocal only steers the choice of q; the residual uses the exact product q S.
+// q S / 4^t from r.  The reciprocal only steers the choice of q; the residual uses the exact product q S.  The
+// residual after the last term is not needed.
 FP4X_DEV void block_terms(float (&v)[16], uint32_t (&lo)[kTerms], uint32_t (&hi)[kTerms], uint32_t (&code)[kTerms]) {
   float up = 1.0f;  // 4^t
 #pragma unroll
@@ -149,23 +168,26 @@ FP4X_DEV void block_terms(float (&v)[16], uint32_t (&lo)[kTerms], uint32_t (&hi)
     }
     const float amax = fmaxf(fmaxf(m0, m1), fmaxf(m2, m3)) * up;
     uint32_t c = 0;
-    float s_down = 0.f, inv_up = 0.f;
+    float neg_s_down = 0.f, inv_up = 0.f;
     if (amax > 0.f) {
       c = e4m3_code_ceil(amax * (1.0f / 6.0f));
       const float s = e4m3_to_f32(c);
       float r;
       asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(s));
       inv_up = r * up;
-      s_down = s * (1.0f / up);
+      neg_s_down = -(s * (1.0f / up));
     }
     code[t] = c;
     uint32_t b[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      b[i] = f32x2_to_e2m1x2(v[2 * i] * inv_up, v[2 * i + 1] * inv_up);
-      const uint32_t h = e2m1x2_to_f16x2(b[i]);
-      v[2 * i] = fmaf(-f16_bits_to_f32(h & 0xffffu), s_down, v[2 * i]);
-      v[2 * i + 1] = fmaf(-f16_bits_to_f32(h >> 16), s_down, v[2 * i + 1]);
+      float y0, y1;
+      mul2(y0, y1, v[2 * i], v[2 * i + 1], inv_up);
+      b[i] = f32x2_to_e2m1x2(y0, y1);
+      if (t + 1 < kTerms) {
+        const uint32_t h = e2m1x2_to_f16x2(b[i]);
+        fma2(v[2 * i], v[2 * i + 1], f16_bits_to_f32(h & 0xffffu), f16_bits_to_f32(h >> 16), neg_s_down);
+      }
     }
     lo[t] = b[0] | (b[1] << 8) | (b[2] << 16) | (b[3] << 24);
     hi[t] = b[4] | (b[5] << 8) | (b[6] << 16) | (b[7] << 24);
