@@ -361,6 +361,74 @@ def time_head(step, reps=5):
     return e0.elapsed_time(e1) * 1e3 / reps
 
 
+def _graph_us(fn, device, reps=5):
+    fn()
+    torch.cuda.synchronize(device)
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            fn()
+    torch.cuda.current_stream(device).wait_stream(s)
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize(device)
+    st = torch.cuda.current_stream(device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(reps):
+        g.replay()
+    e1.record(st)
+    torch.cuda.synchronize(device)
+    del g
+    return e0.elapsed_time(e1) * 1e3 / reps
+
+
+def mixer_sweep(step, ms=(1, 3, 16)):
+    """C3: the fused hyper-connection mixer (W8 down 512x10240 with cast + SiLU, W8 up 10240x512 with the sigmoid
+    gate and stream mean) per M, as a chain over the step's 48 layers of weights (µs per mixer = down + up)."""
+    import fp4x_kernels as F
+    dev = step.dev
+    g = torch.Generator(device=dev)
+    g.manual_seed(13)
+    out = {}
+    for m in ms:
+        streams = torch.randn(m, HCN * HID, device=dev, generator=g).to(torch.bfloat16)
+
+        def run():
+            for L in step.layers:
+                _, bot = step.fx.down(streams, L["qd"], L["sd"], LR, HCN)
+                F.HCFused.up(bot, L["qi"], L["si"], streams, HCN, (8, 64, 8))
+
+        us = _graph_us(run, dev) / len(step.layers)
+        nb = CLASSES["hc_down"] + CLASSES["hc_up"]
+        out[f"hc mixer M={m}"] = {"us": round(us, 2), "GB/s": round(nb / us / 1e3, 1)}
+    return out
+
+
+def head_sweep(step, ms=(1, 3, 16)):
+    """C4: the fast head over the step's 248,320 rows and a 65,536-row draft head (top-64, NVFP4 rescore), per M."""
+    import fp4x_kernels as F
+    dev = step.dev
+    g = torch.Generator(device=dev)
+    g.manual_seed(11)
+    wd = torch.randn(65536, HID, device=dev, generator=g) * 0.02
+    dp, dsn, dgs = F.quantize_nv4(wd)
+    dP, dS = F.quantize_int2(F.dequant_nv4(dp, dsn, dgs), group=16)
+    del wd
+    out = {}
+    for m in ms:
+        h = torch.randn(m, HID, device=dev, generator=g).to(torch.bfloat16)
+        us = _graph_us(lambda: step.head.local(h), dev)
+        nb = head_bytes(m, step.v1 - step.v0)
+        out[f"fast head {step.v1 - step.v0} M={m}"] = {"us": round(us, 2), "GB/s": round(nb / us / 1e3, 1)}
+        us = _graph_us(lambda: F.draft_head(h, dP, dS, dp, dsn, dgs, 64), dev)
+        nb = bytes_int2(65536, HID) + m * 64 * (HID // 2 + HID // 16)
+        out[f"draft head 65536 M={m}"] = {"us": round(us, 2), "GB/s": round(nb / us / 1e3, 1)}
+    return out
+
+
 # ----------------------------------------------------------------------------------------------------------
 # CPU oracle leg (reference arm and cpu_baseline)
 # ----------------------------------------------------------------------------------------------------------
@@ -432,6 +500,45 @@ def cpu_leg(steps, warmup):
 # ----------------------------------------------------------------------------------------------------------
 # per-GEMV sweep at M = 1..16 (the first half of the metric)
 # ----------------------------------------------------------------------------------------------------------
+def gate_batch_sweep(device, g, ms, reps):
+    """The 48 router gates of a step as one batched W8 launch (W8Batch); batches rotate over > 2x L2."""
+    import fp4x_kernels as F
+    n, k, count = GATE, HID, 48
+    nbytes = count * bytes_w8(n, k)
+    copies = max(2, int(2 * 126e6 // nbytes) + 1)
+    weights = [[F.quantize_w8(torch.randn(n, k, device=device, generator=g) * 0.02) for _ in range(count)]
+               for _ in range(copies)]
+    row = {}
+    for m in ms:
+        xs = [torch.randn(m, k, device=device, generator=g).to(torch.bfloat16) for _ in range(count)]
+        batches = [F.W8Batch(xs, [q for q, _ in w], [s_ for _, s_ in w]) for w in weights]
+        for b in batches:
+            b.run()
+        torch.cuda.synchronize(device)
+        s = torch.cuda.Stream(device)
+        s.wait_stream(torch.cuda.current_stream(device))
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(gr, stream=s):
+                for b in batches:
+                    b.run()
+        torch.cuda.current_stream(device).wait_stream(s)
+        gr.replay()
+        torch.cuda.synchronize(device)
+        st = torch.cuda.current_stream(device)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            gr.replay()
+        e1.record(st)
+        torch.cuda.synchronize(device)
+        us = e0.elapsed_time(e1) * 1e3 / (reps * len(batches))
+        row[f"M={m}"] = {"us": round(us, 2), "GB/s": round(nbytes / us / 1e3, 1),
+                         "pct_of_8TBs": round(nbytes / us / 1e3 / 80.0, 1)}
+        del gr, batches
+    return row
+
+
 def gemv_sweep(device, ms=(1, 2, 4, 8, 16), reps=10):
     import fp4x_kernels as F
     g = torch.Generator(device=device)
@@ -445,6 +552,10 @@ def gemv_sweep(device, ms=(1, 2, 4, 8, 16), reps=10):
                           bytes_w6(QKVZ, HID)),
         "nv4 16384x2560": (lambda w: F.quantize_nv4(w), lambda x, a: F.nv4_linear(x, *a), QKVZ, HID,
                            bytes_nv4(QKVZ, HID)),
+        "w8 2560x2560": (lambda w: F.quantize_w8(w), lambda x, a: F.w8_linear(x, *a), HID, HID,
+                         bytes_w8(HID, HID)),
+        "w6 2560x2560": (lambda w: F.quantize_w6(w), lambda x, a: F.w6_linear(x, *a), HID, HID,
+                         bytes_w6(HID, HID)),
     }
     out = {}
     for name, (quant, call, n, k, nbytes) in shapes.items():
@@ -480,6 +591,8 @@ def gemv_sweep(device, ms=(1, 2, 4, 8, 16), reps=10):
         out[name] = row
         del ws
         torch.cuda.empty_cache()
+    out["w8 48 gates 512x2560 (one batched launch)"] = gate_batch_sweep(device, g, ms, reps)
+    torch.cuda.empty_cache()
     return out
 
 
@@ -600,6 +713,7 @@ def native_arm(args):
         top_bytes, top_us = CLASSES[top], per_class[top]
     achieved = top_bytes / (top_us * 1e-6) / 1e9
 
+    heads = head_sweep(step) | mixer_sweep(step) if (world == 1 and not args.no_sweep) else None
     sweep = gemv_sweep(dev) if (world == 1 and not args.no_sweep) else None
 
     if rank == 0:
@@ -636,6 +750,8 @@ def native_arm(args):
         }
         if sweep is not None:
             line["gemv_sweep"] = sweep
+        if heads is not None:
+            line["head_and_mixer_sweep"] = heads
         print(json.dumps(line), flush=True)
     barrier(world, dev)
     step.graph = None
