@@ -204,6 +204,7 @@ struct Plan {
   int KPW, KP, KC, NCH, CPP, RT, NS, SMAX, whole;
   int BI0, BI1, NB0, SB, STG, off_p1, off_sc, XP;
   int smem_x, smem_misc, smem_scr, smem_xraw, smem_comb, smem_red, smem_total;
+  int xdirect;  // 16-token plans: the raw activation panel stays in global memory
   int cluster;
   size_t ws_bytes;
   int64_t counters;
@@ -260,7 +261,9 @@ static bool make_cluster_plan(int fmt, int64_t M, int64_t N, int64_t K, int grou
     c.STG = round_up(c.off_sc + kRB * c.SB, 1024);
     c.XP = (kpw / 16) * 32 + 32;
     const int red_bytes = (KP - 1) * kRW * 32 * c.NT * 16;
-    const int xbytes = round_up(c.MP * c.XP, 16) + (int)M * kpw * 2;
+    c.xdirect = 0;
+    const int raw = (int)M * kpw * 2;
+    const int xbytes = round_up(c.MP * c.XP, 16) + raw;
     const int fixed = xbytes + misc + comb_bytes + red_bytes + 1024;
     const int ctas = base.RT * KP;
     const int cap = ctas > dv.sms ? dv.smem_sm / 2 - 2048 : dv.smem_optin;
@@ -276,7 +279,7 @@ static bool make_cluster_plan(int fmt, int64_t M, int64_t N, int64_t K, int grou
     c.smem_misc = c.smem_x + round_up(c.MP * c.XP, 16);
     c.smem_scr = c.smem_misc + misc;
     c.smem_xraw = c.smem_scr;
-    c.smem_comb = c.smem_xraw + round_up((int)M * kpw * 2, 16);
+    c.smem_comb = c.smem_xraw + round_up(raw, 16);
     c.smem_red = c.smem_comb + comb_bytes;
     c.smem_total = c.smem_red + red_bytes + 1024;
     c.ws_bytes = 0;
@@ -315,9 +318,15 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
   const int cap1 = dv.smem_optin;
   const int cap2 = dv.smem_sm / 2 - 2048;  // two CTAs per SM (1 KB reserved per CTA, 1 KB alignment slack)
 
+  // 16-token plans: the raw activation panel (M x panel x 2 bytes) may stay in global memory (staging then reads
+  // it from L2) when keeping it in shared memory would force the K dimension into more than two panels.
   bool found = false;
-  double best_score = -1e30;
   Plan best = pl;
+  for (int direct = 0; direct <= (pl.NT == 2 ? 1 : 0); ++direct) {
+  if (direct && found && best.KP <= 2) break;
+  bool found_d = false;
+  double best_score = -1e30;
+  Plan best_d = pl;
   for (int kpw = (int)K; kpw >= 64; --kpw) {
     if (K % kpw) continue;
     if (whole && kpw != K) break;
@@ -337,7 +346,8 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
     c.off_sc = c.off_p1 + kRB * c.BI1;
     c.STG = round_up(c.off_sc + kRB * c.SB, 1024);
     c.XP = (kpw / 16) * 32 + 32;
-    const int xbytes = round_up(c.MP * c.XP, 16) + (int)M * kpw * 2;  // permuted panel + raw bf16 panel
+    c.xdirect = direct;
+    const int xbytes = round_up(c.MP * c.XP, 16) + (c.xdirect ? 0 : (int)M * kpw * 2);  // permuted + raw panels
     const int fixed = xbytes + misc + scr_bytes + comb_bytes + 1024;
     for (int cps = 2; cps >= 1; --cps) {
       const int cap = cps == 2 ? cap2 : cap1;
@@ -358,11 +368,16 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
         best_score = score;
         c.NS = ns;
         c.CPP = cps;  // CTAs per SM for now
-        best = c;
-        found = true;
+        best_d = c;
+        found_d = true;
       }
       break;
     }
+  }
+  if (found_d && (!found || best_d.KP < best.KP)) {
+    best = best_d;
+    found = true;
+  }
   }
   if (!found) return fail(FP4X_ERR_UNSUPPORTED, "shape needs more shared memory than available");
   pl = best;
@@ -376,7 +391,7 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
   pl.smem_misc = pl.smem_x + round_up(pl.MP * pl.XP, 16);
   pl.smem_scr = pl.smem_misc + misc;
   pl.smem_xraw = pl.smem_scr + round_up(scr_bytes, 16);
-  pl.smem_comb = pl.smem_xraw + round_up((int)M * pl.KPW * 2, 16);
+  pl.smem_comb = pl.smem_xraw + round_up(pl.xdirect ? 0 : (int)M * pl.KPW * 2, 16);
   pl.smem_total = pl.smem_comb + comb_bytes + 1024;
   pl.SMAX = whole ? 1 : (int)((int64_t)(pl.NCH - 1) * pl.CPP / Up) + 2;
   if (pl.SMAX > pl.CPP) pl.SMAX = pl.CPP;
@@ -442,6 +457,7 @@ static void fill_args(const Plan& pl, GemvArgs& a) {
   a.BI0 = pl.BI0; a.BI1 = pl.BI1; a.NB0 = pl.NB0; a.SB = pl.SB; a.STG = pl.STG;
   a.off_p1 = pl.off_p1; a.off_sc = pl.off_sc; a.XP = pl.XP;
   a.smem_x = pl.smem_x; a.smem_misc = pl.smem_misc; a.smem_scr = pl.smem_scr; a.smem_xraw = pl.smem_xraw;
+  a.xdirect = pl.xdirect;
   a.smem_comb = pl.smem_comb;
   a.cluster = pl.cluster; a.smem_red = pl.smem_red;
 }
