@@ -83,9 +83,9 @@ int fp4x_mx8_linear(const void* x, int64_t x_stride, const void* w, const void* 
 /* MXFP8 GEMV that allocates nothing and takes no scratch (no counterpart in the reference).  It always runs the
  * register-decode split-K kernel; fp4x_mx8_linear sends M <= 8 at 8192 rows or more to the tensor-core kernel, so
  * the two agree to fp32 summation order.  For callers that cannot hand the library a workspace or allocate device
- * memory at call time, such as a host runtime without a caching allocator.  The split-K scratch is a static device array
- * of the library: 8 MiB of partial tiles and 32768 int32 arrival counters per device.  Shapes whose plan needs more
- * are rejected with FP4X_ERR_WORKSPACE.  The first call on each device resolves the scratch address
+ * memory at call time, such as a host runtime without a caching allocator.  The split-K scratch is a static
+ * device array of the library: 8 MiB of partial tiles and 32768 int32 arrival counters per device.  Shapes whose
+ * plan needs more are rejected with FP4X_ERR_WORKSPACE.  The first call on each device resolves the scratch address
  * (cudaGetSymbolAddress), so make it before capturing any stream on that device.  The counters are zero when the
  * library loads and each completed call leaves them zero.  All calls on one device share the scratch, so calls
  * that may run at the same time (other streams or threads, without ordering) race: order them on one stream. */
