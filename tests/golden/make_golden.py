@@ -7,8 +7,9 @@ semantics evaluated with torch on CPU: the kernel's bf16 weights (the reference'
 per-group product the Triton kernel forms at the cited lines) times `x.float()`, as the reference's own tuners do
 (`x/probes/tune.py:27,33`).
 
-Run from the repository root:  python tests/golden/make_golden.py [path/to/reference/x/fp4x_kernels.py]
-The fixtures are committed; this script is only needed to regenerate them.
+Run from the repository root:  python tests/golden/make_golden.py path/to/reference/x/fp4x_kernels.py
+(or set FP4X_REFERENCE_KERNELS to that path).  The fixtures are committed; this script is only needed to
+regenerate them.
 """
 import importlib.util
 import os
@@ -18,7 +19,6 @@ import numpy as np
 import torch
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-DEFAULT_REF = "/root/reference/x/fp4x_kernels.py"
 
 
 def load_ref(path):
@@ -33,7 +33,9 @@ def bf16_bits(t):
 
 
 def main():
-    ref_path = sys.argv[1] if len(sys.argv) > 1 else DEFAULT_REF
+    ref_path = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("FP4X_REFERENCE_KERNELS")
+    if not ref_path:
+        raise SystemExit("usage: make_golden.py path/to/reference/x/fp4x_kernels.py (or set FP4X_REFERENCE_KERNELS)")
     R = load_ref(ref_path)
     g = torch.Generator().manual_seed(0)
     out = {}

@@ -3,7 +3,7 @@ draft heads, and the merge of a vocab-sharded head.
 
 Set semantics: the top-C set is defined on fp32 coarse values with the total order (value desc, index asc).
 Against the oracle's float64 coarse values, indices whose value lies within the fp32 accumulation bound of the
-C-th value are ambiguous (not judged); all others must agree.  Against the kernel's own fp32 coarse values the
+C-th value are ambiguous (not checked); all others must agree.  Against the kernel's own fp32 coarse values the
 selection must be exact.
 """
 import numpy as np
