@@ -502,8 +502,9 @@ static int launch_nv4_tc(const tc::Args& a, unsigned grid, int smem_total, void*
   auto kern = tc::nv4_tc_kernel<MT>;
   cudaError_t e = ensure_smem_attr((const void*)kern, smem_total);
   if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
-  return check_launch(launch_pdl(kern, dim3(grid), dim3(tc::kThreads), (size_t)smem_total, (cudaStream_t)stream, a),
-                      "nv4 tcgen05 launch");
+  return check_launch(
+      launch_pdl(kern, dim3(grid), dim3(tc::nv_threads(MT)), (size_t)smem_total, (cudaStream_t)stream, a),
+      "nv4 tcgen05 launch");
 }
 
 // NVFP4 on tcgen05 block-scaled MMAs (fp4x_tc.cuh): M <= 8 tokens, at least 64 row blocks of 128, K a multiple

@@ -16,12 +16,12 @@
 // range; after T = 6 terms the remainder is below 2^-13 of the token's largest element (the products themselves are
 // exact and accumulate in fp32).  The epilogue recombines the term columns with the factors 2^(e0 - 2t).
 //
-// Roles (384 threads): warp 0 streams weight tiles and their scale tiles (TMA); warp 1 owns the tensor memory and
-// one of its lanes issues the MMAs; warps 2..7 turn the activations into e2m1 terms after the grid-dependency wait,
-// slab by slab (256 k), so the MMAs of the first slabs start while later slabs are still being prepared; warps 8..11
-// (tensor-memory subpartitions 0..3) write each stage's A scales and each slab's B scales into tensor memory from
-// registers, running ahead of the MMAs, and then run the epilogue.  Every wait is bounded; a failed wait records an
-// error and the kernel still releases its tensor memory.
+// Roles (384 threads; 576 at 8 tokens): warp 0 streams weight tiles and their scale tiles (TMA); warp 1 owns the
+// tensor memory and one of its lanes issues the MMAs; warps 2..7 (and 12..17 at 8 tokens) turn the activations into
+// e2m1 terms after the grid-dependency wait, slab by slab (256 k), so the MMAs of the first slabs start while later
+// slabs are still being prepared; warps 8..11 (tensor-memory subpartitions 0..3) write each stage's A scales and
+// each slab's B scales into tensor memory from registers, running ahead of the MMAs, and then run the epilogue.
+// Every wait is bounded; a failed wait records an error and the kernel still releases its tensor memory.
 #pragma once
 #include <cuda.h>
 
@@ -31,6 +31,10 @@ namespace fp4x {
 namespace tc {
 
 constexpr int kThreads = 384;
+// NVFP4 at 8 tokens: six more term-preparation warps (12..17), so each SM sub-partition runs three of them.  At
+// 8 tokens this took a 16384 x 2560 GEMV from 14.9 to 12.9 us; at 1-4 tokens it made no difference or was slower.
+__host__ __device__ constexpr int nv_prep_extra(int mt) { return mt >= 8 ? 6 : 0; }
+__host__ __device__ constexpr int nv_threads(int mt) { return kThreads + 32 * nv_prep_extra(mt); }
 constexpr int kRows = 128;          // MMA M
 constexpr int kKC = 256;            // k per stage (128 bytes of e2m1 per row)
 constexpr int kMaxStages = 8;
@@ -203,7 +207,7 @@ FP4X_DEV uint32_t b_offset(int NB, int n, int k) {
 }
 
 template <int MT>
-__global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_constant__ Args A) {
+__global__ void __launch_bounds__(nv_threads(MT), 1) nv4_tc_kernel(const __grid_constant__ Args A) {
   constexpr int NBT = (kTerms * MT + 15) / 16 * 16;
   constexpr int NACC = NBT <= 32 ? 4 : 2;  // accumulators of NBT columns within the 128 columns at kColD
   constexpr int kBlkPerSlab = MT * 16;     // 16-element activation blocks per 256-k slab (all tokens)
@@ -285,7 +289,7 @@ __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_consta
       tc_commit(dfull);  // completes when every MMA issued above has finished
     }
     __syncwarp();
-  } else if (warp >= 8) {
+  } else if (warp >= 8 && warp < 12) {
     // ---------------- scale writers (subpartition warp - 8), then the epilogue ----------------
     const int sub = warp - 8;
     const uint32_t tsub = tmem + ((uint32_t)(32 * sub) << 16);
@@ -357,8 +361,8 @@ __global__ void __launch_bounds__(kThreads, 1) nv4_tc_kernel(const __grid_consta
     }
     tc_fence_before();
   } else {
-    // ---------------- activations -> e2m1 terms (warps 2..7), slab by slab ----------------
-    const int ptid = threadIdx.x - 64, pthreads = 192;
+    // ---------------- activations -> e2m1 terms (warps 2..7, 12..), slab by slab ----------------
+    const int ptid = warp < 8 ? threadIdx.x - 64 : threadIdx.x - 192, pthreads = 192 + 32 * nv_prep_extra(MT);
     pdl_wait();
     const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(base + A.smem_xraw);
     if (ptid == 0) {
