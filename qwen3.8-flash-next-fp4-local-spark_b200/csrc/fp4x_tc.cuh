@@ -16,8 +16,8 @@
 // range; after T = 6 terms the remainder is below 2^-13 of the token's largest element (the products themselves are
 // exact and accumulate in fp32).  The epilogue recombines the term columns with the factors 2^(e0 - 2t).
 //
-// Roles (384 threads; 576 at 8 tokens): warp 0 streams weight tiles and their scale tiles (TMA); warp 1 owns the
-// tensor memory and one of its lanes issues the MMAs; warps 2..7 (and 12..17 at 8 tokens) turn the activations into
+// Roles (384 threads; 576 at 5-8 tokens): warp 0 streams weight tiles and their scale tiles (TMA); warp 1 owns the
+// tensor memory and one of its lanes issues the MMAs; warps 2..7 (and 12..17 at 5-8 tokens) turn the activations into
 // e2m1 terms after the grid-dependency wait, slab by slab (256 k), so the MMAs of the first slabs start while later
 // slabs are still being prepared; warps 8..11 (tensor-memory subpartitions 0..3) write each stage's A scales and
 // each slab's B scales into tensor memory from registers, running ahead of the MMAs, and then run the epilogue.
@@ -31,9 +31,10 @@ namespace fp4x {
 namespace tc {
 
 constexpr int kThreads = 384;
-// NVFP4 at 8 tokens: six more term-preparation warps (12..17), so each SM sub-partition runs three of them.  At
-// 8 tokens this took a 16384 x 2560 GEMV from 14.9 to 12.9 us; at 1-4 tokens it made no difference or was slower.
-__host__ __device__ constexpr int nv_prep_extra(int mt) { return mt >= 8 ? 6 : 0; }
+// NVFP4 at 5-8 tokens: six more term-preparation warps (12..17), so each SM sub-partition runs three of them.  On a
+// 16384 x 2560 GEMV this took 5 / 6 / 7 / 8 tokens from 11.2 / 12.4 / 14.0 / 14.9 us to 10.7 / 11.4 / 12.1 / 12.8 us;
+// at 1-4 tokens it made no difference or was slower.
+__host__ __device__ constexpr int nv_prep_extra(int mt) { return mt >= 5 ? 6 : 0; }
 __host__ __device__ constexpr int nv_threads(int mt) { return kThreads + 32 * nv_prep_extra(mt); }
 constexpr int kRows = 128;          // MMA M
 constexpr int kKC = 256;            // k per stage (128 bytes of e2m1 per row)
