@@ -253,8 +253,11 @@ class DecodeStep:
         h = self.h0
         for L in self.layers:
             h = self.layer(L, h)
+        if self.world == 1:  # one shard: the head's own argmax is the answer, no merge
+            coarse, exact, gidx, _, amax = self.head.local(h, argmax=True)
+            return coarse, exact, gidx, amax
         coarse, exact, gidx, _ = self.head.local(h)
-        return coarse, exact, gidx
+        return coarse, exact, gidx, None
 
     def capture(self):
         """Capture the layers and the local head in one graph; returns the number of library kernels per step."""
@@ -275,17 +278,44 @@ class DecodeStep:
     def step(self):
         """One decode step: graph replay, then (N > 1) the candidate exchange and merge; returns (idx, argmax)."""
         self.graph.replay()
-        coarse, exact, gidx = self.local
+        coarse, exact, gidx, amax = self.local
         if self.world == 1:
-            co, ex, gi = coarse[None], exact[None], gidx[None]
-        else:
-            from fp4x_shard import gather_candidates
-            co, ex, gi = gather_candidates(coarse, exact, gidx)
+            return gidx, amax
+        from fp4x_shard import gather_candidates
+        co, ex, gi = gather_candidates(coarse, exact, gidx)
         idx, _, _, amax = self.F.head_merge(co, ex, gi, VOCAB)
         return idx, amax
 
     def merge_launches(self):
-        return 1
+        return 0 if self.world == 1 else 1
+
+    def exchange_timings(self, reps=20):
+        """Device times (µs) of the pieces of the sharded head: the local head alone, the NCCL all-gather of the
+        packed [3, M, C] fp32 candidates, and the merge kernel (every rank takes the same collective steps)."""
+        from fp4x_shard import gather_candidates
+        coarse, exact, gidx, _ = self.local
+        st = torch.cuda.current_stream(self.dev)
+        out = {"head_us": round(time_head(self), 2)}
+        if self.world == 1:
+            out.update({"allgather_us": 0.0, "merge_us": 0.0})
+            return out
+        for _ in range(3):
+            co, ex, gi = gather_candidates(coarse, exact, gidx)
+        torch.cuda.synchronize(self.dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(st)
+        for _ in range(reps):
+            co, ex, gi = gather_candidates(coarse, exact, gidx)
+        e1.record(st)
+        torch.cuda.synchronize(self.dev)
+        out["allgather_us"] = round(e0.elapsed_time(e1) * 1e3 / reps, 2)
+        e0.record(st)
+        for _ in range(reps):
+            self.F.head_merge(co, ex, gi, VOCAB)
+        e1.record(st)
+        torch.cuda.synchronize(self.dev)
+        out["merge_us"] = round(e0.elapsed_time(e1) * 1e3 / reps, 2)
+        return out
 
 
 def time_graph_class(step, name, reps=5):
@@ -338,14 +368,15 @@ def time_graph_class(step, name, reps=5):
 def time_head(step, reps=5):
     """Average device time of the local fast head (coarse pass + top-512 + rescore)."""
     h = step.h0
-    step.head.local(h)
+    one = step.world == 1
+    step.head.local(h, argmax=one)
     torch.cuda.synchronize(step.dev)
     s = torch.cuda.Stream(step.dev)
     s.wait_stream(torch.cuda.current_stream(step.dev))
     g = torch.cuda.CUDAGraph()
     with torch.cuda.stream(s):
         with torch.cuda.graph(g, stream=s):
-            step.head.local(h)
+            step.head.local(h, argmax=one)
     torch.cuda.current_stream(step.dev).wait_stream(s)
     for _ in range(3):
         g.replay()
@@ -433,68 +464,108 @@ def head_sweep(step, ms=(1, 3, 16)):
 # CPU oracle leg (reference arm and cpu_baseline)
 # ----------------------------------------------------------------------------------------------------------
 class CpuSample:
-    """One layer of the step plus 1/64 of the head rows (and the M x 512 rescore rows) through the numpy oracle."""
+    """The reference's CPU path (torch eager: dequantize, then x.float() @ W.T; oracle/fp4x_eager.py) on a bounded
+    sample of the step: one layer plus 1/64 of the head rows and the M x 512 MXFP8 rescore rows.  Two variants:
+    dequantize on every call (what an eager forward does) and the matmul alone against weights dequantized once."""
 
     HEAD_FRACTION = 64
 
     def __init__(self, m=3, seed=0):
         sys.path.insert(0, os.path.join(ROOT, "oracle"))
-        import fp4x_oracle as O
-        self.O = O
-        rng = np.random.default_rng(seed)
+        import fp4x_eager as E
+        import fp4x_kernels as F
+        self.E = E
+        self.threads_used = os.cpu_count() or 1
+        torch.set_num_threads(self.threads_used)
+        g = torch.Generator().manual_seed(seed)
 
         def w(n, k):
-            return (rng.standard_normal((n, k), dtype=np.float32) * 0.02)
+            return torch.randn(n, k, generator=g) * 0.02
 
-        self.nv4 = O.quantize_nv4(w(QKVZ, HID))
-        self.w6a = O.quantize_w6(w(HID, W6_IN))
-        self.w6b = O.quantize_w6(w(W6_IN, HID))
-        self.gate = O.quantize_w8(w(GATE, HID))
-        self.qd, self.sd = O.quantize_w8(w(LR, HCN * HID))
-        self.qu, self.su = O.quantize_w8(w(HCN * HID, LR))
+        self.nv4 = F.quantize_nv4(w(QKVZ, HID))
+        self.w6a = F.quantize_w6(w(HID, W6_IN))
+        self.w6b = F.quantize_w6(w(W6_IN, HID))
+        self.gate = F.quantize_w8(w(GATE, HID))
+        self.qd, self.sd = F.quantize_w8(w(LR, HCN * HID))
+        self.qu, self.su = F.quantize_w8(w(HCN * HID, LR))
         rows = VOCAB // self.HEAD_FRACTION
         self.head_rows = rows
-        self.w8, self.s8 = O.quantize_mx8(w(rows, HID))
-        self.P, self.S = O.quantize_int2(O.mx8_dequant(self.w8, self.s8), 16)
-        self.h = O.bf16(rng.standard_normal((m, HID)).astype(np.float32))
-        self.streams = O.bf16(rng.standard_normal((m, HCN * HID)).astype(np.float32))
+        self.w8, self.s8 = F.quantize_mx8(w(rows, HID))
+        self.P, self.S = F.quantize_int2(F.mx8_dequant(self.w8, self.s8), group=16)
+        self.h = torch.randn(m, HID, generator=g).to(torch.bfloat16)
+        self.streams = torch.randn(m, HCN * HID, generator=g).to(torch.bfloat16)
         self.m = m
         self.bytes = LAYER_BYTES + bytes_int2(rows, HID) + bytes_rescore(m, CAND, HID)
+        self.pre = None
 
-    def run(self):
-        O = self.O
-        q = O.nv4_linear(self.h, *self.nv4)
-        o = O.w6_linear(O.bf16(q[:, :W6_IN]), *self.w6a)
-        O.w6_linear(O.bf16(o), *self.w6b)
-        O.w8_linear(self.h, *self.gate)
-        _, _, h = O.hc_mixer(self.streams, self.qd, self.sd, self.qu, self.su, LR, HCN)
-        O.fast_head(O.bf16(h), self.P, self.S, self.w8, self.s8, min(CAND, self.head_rows))
+    def _weights(self):
+        E = self.E
+        P, S, gs = self.nv4
+        return {"nv4": (E.nv4_dequant(P, S), gs), "w6a": E.w6_dequant(*self.w6a), "w6b": E.w6_dequant(*self.w6b),
+                "gate": E.w8_dequant(*self.gate), "down": E.w8_dequant(self.qd, self.sd),
+                "up": E.w8_dequant(self.qu, self.su), "int2": E.int2_dequant(self.P, self.S)}
 
-    @staticmethod
-    def threads():
-        try:
-            from threadpoolctl import threadpool_info
-            n = [i.get("num_threads", 1) for i in threadpool_info()]
-            return max(n) if n else 1
-        except Exception:
-            return 1
+    def run(self, predequantized=False):
+        E = self.E
+        if predequantized:
+            if self.pre is None:
+                self.pre = self._weights()
+            W = self.pre
+        else:
+            W = self._weights()
+        wq, gs = W["nv4"]
+        q = E.matmul(self.h, wq) * gs
+        o = E.matmul(q[:, :W6_IN].to(torch.bfloat16), W["w6a"])
+        E.matmul(o.to(torch.bfloat16), W["w6b"])
+        E.matmul(self.h, W["gate"])
+        di = E.matmul(self.streams, W["down"]).to(torch.bfloat16)
+        t = (di.float() / HCN).to(torch.bfloat16).float()
+        bot = (t * torch.sigmoid(t)).to(torch.bfloat16)
+        gl = E.matmul(bot, W["up"]).to(torch.bfloat16).float()
+        gate = torch.sigmoid(gl).to(torch.bfloat16).float()
+        nrm = self.streams.float()
+        prods = [(nrm[:, s * HID:(s + 1) * HID] * gate[:, s * HID:(s + 1) * HID]).to(torch.bfloat16).float()
+                 for s in range(HCN)]
+        h = (((prods[0] + prods[1]) + (prods[2] + prods[3])) / HCN).to(torch.bfloat16)
+        coarse = E.matmul(h, W["int2"])
+        idx = torch.topk(coarse, min(CAND, self.head_rows), dim=1).indices
+        for r in range(self.m):
+            rows = E.mx8_dequant(self.w8[idx[r]], self.s8[idx[r]])
+            exact = rows @ h[r].float()
+            coarse[r, idx[r]] = exact
+        return coarse.argmax(dim=1)
 
-    def describe(self):
+    def describe(self, variant):
+        how = ("dequantize on every call" if variant == "dequant_per_call"
+               else "weights dequantized to fp32 once, matmul only")
         return (f"one layer of the step (NVFP4 16384x2560, W6 2560x4096, W6 4096x2560, W8 gate 512x2560, HC mixer "
                 f"512x10240 + 10240x512) + fast head on {self.head_rows} of {VOCAB} rows with the M={self.m} x 512 "
-                f"MXFP8 rescore; numpy oracle (dequantize, float64 matmul)")
+                f"MXFP8 rescore; torch eager restatement of the reference's CPU path ({how}), "
+                f"{self.threads_used} threads")
 
 
-def cpu_leg(steps, warmup):
-    """Time the oracle sample: returns (GB/s, seconds per sample, sample object)."""
-    sample = CpuSample()
+def cpu_leg(steps, warmup, predequantized=False, sample=None):
+    """Time the CPU sample: returns (GB/s, seconds per sample, sample object)."""
+    sample = sample or CpuSample()
     for _ in range(warmup):
-        sample.run()
+        sample.run(predequantized)
     t0 = time.perf_counter()
     for _ in range(steps):
-        sample.run()
+        sample.run(predequantized)
     dt = (time.perf_counter() - t0) / steps
     return sample.bytes / dt / 1e9, dt, sample
+
+
+def cpu_baseline_record(steps=1, warmup=0):
+    """Both CPU variants on the host cores; the line's value is the per-call-dequantize variant."""
+    gbs, dt, sample = cpu_leg(steps, warmup, predequantized=False)
+    gbs2, dt2, _ = cpu_leg(max(steps, 3), 1, predequantized=True, sample=sample)
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": sample.threads_used,
+            "kind": "port (torch eager restatement of the reference's dequantize + matmul; the reference has no "
+                    "installable package)",
+            "sample": sample.describe("dequant_per_call") + f"; {dt:.2f} s per sample",
+            "variants": {"dequant_per_call": {"GB/s": round(gbs, 3), "s_per_sample": round(dt, 3)},
+                         "predequantized_fp32": {"GB/s": round(gbs2, 3), "s_per_sample": round(dt2, 4)}}}
 
 
 # ----------------------------------------------------------------------------------------------------------
@@ -627,11 +698,13 @@ def reference_arm(args):
     line = {
         "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3, 2), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f64 (numpy oracle)", "data": "synthetic",
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32 (torch eager, dequantize then matmul)",
+        "data": "synthetic",
         "config": {"workload": "C5 synthetic M=3 decode step, bounded CPU sample", "M": 3,
-                   "sample": sample.describe()},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": CpuSample.threads(), "kind": "port",
-                         "sample": sample.describe()},
+                   "sample": sample.describe("dequant_per_call")},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": "GB/s", "cores": sample.threads_used,
+                         "kind": "port (torch eager restatement of the reference's dequantize + matmul)",
+                         "sample": sample.describe("dequant_per_call")},
         "e2e": {"value": round(gbs, 3), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -702,7 +775,9 @@ def native_arm(args):
 
     # dominant kernel class, timed alone
     per_class = {name: time_graph_class(step, name) for name in CLASSES}
-    head_us = time_head(step)
+    exchange = step.exchange_timings()
+    exchange = {k: max_over_ranks(v, world, dev) for k, v in exchange.items()}
+    head_us = exchange["head_us"]
     shares = {name: us * args.layers for name, us in per_class.items()}
     shares["fast_head"] = head_us
     top = max(shares, key=shares.get)
@@ -719,9 +794,7 @@ def native_arm(args):
     if rank == 0:
         cpu = None
         if world == 1 and not args.no_cpu:
-            gbs, dt, sample = cpu_leg(1, 0)
-            cpu = {"value": round(gbs, 3), "unit": "GB/s", "cores": CpuSample.threads(), "kind": "port",
-                   "sample": sample.describe() + f"; {dt:.1f} s per sample"}
+            cpu = cpu_baseline_record()
         line = {
             "metric": METRIC, "value": round(value, 1), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": "weak",
@@ -740,6 +813,7 @@ def native_arm(args):
                          "frac": round(achieved / peak, 4), "traffic": traffic_for(top),
                          "per_launch_us": round(top_us, 3), "bytes_per_launch": top_bytes},
             "class_us": {k: round(v, 2) for k, v in per_class.items()} | {"fast_head": round(head_us, 2)},
+            "sharded_head_us": exchange,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "ms_per_step": round(ms_e2e, 4),
                     "h2d_bytes_per_step": h_host.numel() * 2 + s_host.numel() * 2,
@@ -761,6 +835,76 @@ def native_arm(args):
     return 0
 
 
+PROFILE_CLASSES = ("nv4_qkvz", "w6_2560x4096", "w6_4096x2560", "w8_gate", "hc_down", "hc_up", "w6_16384x2560",
+                   "w8_16384x2560", "mx8_16384x2560", "gate_batch48", "fast_head")
+
+
+def profile_arm(args):
+    """Small eager runs of single kernel classes for ncu captures: each named class is launched `--launches` times
+    on freshly quantized weights of its shape (one layer's worth; the head at its full 248,320 rows), in the order
+    given.  Prints one line per class and exits; no timing is reported."""
+    import fp4x_kernels as F
+    from fp4x_shard import ShardedFastHead
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (the CUDA path is the only path)")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    m = args.m
+
+    def w(n, k):
+        return torch.randn(n, k, device=dev, generator=g) * 0.02
+
+    def x(k):
+        return torch.randn(m, k, device=dev, generator=g).to(torch.bfloat16)
+
+    names = PROFILE_CLASSES if args.kernel_class == "all" else tuple(args.kernel_class.split(","))
+    for name in names:
+        if name == "nv4_qkvz":
+            a, h = F.quantize_nv4(w(QKVZ, HID)), x(HID)
+            run = lambda: F.nv4_linear(h, *a)  # noqa: E731
+        elif name in ("w6_2560x4096", "w6_4096x2560", "w6_16384x2560"):
+            n, k = {"w6_2560x4096": (HID, W6_IN), "w6_4096x2560": (W6_IN, HID), "w6_16384x2560": (QKVZ, HID)}[name]
+            a, h = F.quantize_w6(w(n, k)), x(k)
+            run = lambda: F.w6_linear(h, *a)  # noqa: E731
+        elif name in ("w8_gate", "w8_16384x2560"):
+            n = GATE if name == "w8_gate" else QKVZ
+            a, h = F.quantize_w8(w(n, HID)), x(HID)
+            run = lambda: F.w8_linear(h, *a)  # noqa: E731
+        elif name == "mx8_16384x2560":
+            a, h = F.quantize_mx8(w(QKVZ, HID)), x(HID)
+            run = lambda: F.mx8_linear(h, *a, None)  # noqa: E731
+        elif name == "hc_down":
+            fx = F.HCFused(dev, n_down=LR)
+            qd, sd = F.quantize_w8(w(LR, HCN * HID))
+            st = x(HCN * HID)
+            run = lambda: fx.down(st, qd, sd, LR, HCN)  # noqa: E731
+        elif name == "hc_up":
+            qi, si = F.HCFused.interleave_up(*F.quantize_w8(w(HCN * HID, LR)), HCN, 8)
+            st, bot = x(HCN * HID), x(LR)
+            run = lambda: F.HCFused.up(bot, qi, si, st, HCN, (8, 64, 8))  # noqa: E731
+        elif name == "gate_batch48":
+            batch = F.W8Batch([x(HID) for _ in range(48)], *zip(*[F.quantize_w8(w(GATE, HID)) for _ in range(48)]))
+            run = batch.run
+        elif name == "fast_head":
+            codes, sc = F.quantize_mx8(w(VOCAB, HID))
+            P, S = F.quantize_int2(F.mx8_dequant(codes, sc), group=16)
+            head = ShardedFastHead(P, S, codes, sc, VOCAB, 0, 1, C=CAND)
+            del codes, sc
+            h = x(HID)
+            run = lambda: head.local(h, argmax=True)  # noqa: E731
+        else:
+            raise SystemExit(f"unknown kernel class {name}; one of {', '.join(PROFILE_CLASSES)} or all")
+        for _ in range(args.launches):
+            run()
+        torch.cuda.synchronize(dev)
+        print(f"{name}: {args.launches} launches at M={m}", flush=True)
+        del run
+        torch.cuda.empty_cache()
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -771,6 +915,9 @@ def main():
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-sweep", action="store_true", help="skip the per-GEMV M=1..16 sweep (single GPU only)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle baseline")
+    ap.add_argument("--kernel-class", default=None,
+                    help="profiling aid: launch only these kernel classes (comma list or 'all') and exit")
+    ap.add_argument("--launches", type=int, default=3, help="launches per class with --kernel-class")
     args = ap.parse_args()
     if args.warmup < 3:
         ap.error("--warmup must be at least 3")
@@ -778,6 +925,8 @@ def main():
     if world != args.gpus:
         if world == 1 and args.gpus > 1:
             ap.error("--gpus N > 1 runs under torchrun (one process per GPU)")
+    if args.kernel_class:
+        return profile_arm(args)
     return reference_arm(args) if args.impl == "reference" else native_arm(args)
 
 

@@ -62,8 +62,20 @@ const char* fp4x_last_error_message(void);
 int64_t fp4x_launch_count(void);
 
 /* Reads (and optionally clears) the device error word that bounded waits set when they give up.
- * Synchronizes `stream`.  Returns FP4X_OK when the word is zero, FP4X_ERR_DEVICE otherwise. */
+ * Synchronizes `stream`.  Returns FP4X_OK when the word is zero, FP4X_ERR_DEVICE otherwise.
+ * A kernel whose wait gave up may leave arrival counters mid-count.  Clearing a non-zero word therefore also zeroes
+ * the library's static counters (those of fp4x_mx8_linear_noalloc); counter arrays the caller passed in must be
+ * zeroed by the caller before they are used again. */
 int fp4x_device_error(void* stream, int clear, int* code_out);
+
+/* Test hook (no reference counterpart): launches one CTA that waits on an mbarrier no thread arrives on, through
+ * the library's bounded wait with a limit of limit_ns (1e3..1e9); the wait gives up, records its code in the device
+ * error word and the kernel returns, so the next fp4x_device_error reports FP4X_ERR_DEVICE.  Nothing faults. */
+int fp4x_test_expire_wait(int64_t limit_ns, void* stream);
+
+/* Test hook (no reference counterpart): writes `value` into static arrival counter `index` of the current device
+ * (the scratch of fp4x_mx8_linear_noalloc), to reproduce what a wait that gave up leaves behind.  Synchronous. */
+int fp4x_test_set_static_counter(int64_t index, int32_t value, void* stream);
 
 /* Scratch needed by one GEMV-family call: workspace bytes and number of int32 counters.
  * fmt: FP4X_FMT_*; batch: number of matrices of a batched call (1 otherwise); group: INT2 scale group. */
@@ -87,7 +99,8 @@ int fp4x_mx8_linear(const void* x, int64_t x_stride, const void* w, const void* 
  * device array of the library: 8 MiB of partial tiles and 32768 int32 arrival counters per device.  Shapes whose
  * plan needs more are rejected with FP4X_ERR_WORKSPACE.  The first call on each device resolves the scratch address
  * (cudaGetSymbolAddress), so make it before capturing any stream on that device.  The counters are zero when the
- * library loads and each completed call leaves them zero.  All calls on one device share the scratch, so calls
+ * library loads and each completed call leaves them zero; after a call that reported FP4X_ERR_DEVICE (a bounded wait
+ * gave up), fp4x_device_error(stream, 1, ...) zeroes them again.  All calls on one device share the scratch, so calls
  * that may run at the same time (other streams or threads, without ordering) race: order them on one stream. */
 int fp4x_mx8_linear_noalloc(const void* x, int64_t x_stride, const void* w, const void* s, void* out,
                             int64_t out_stride, int out_dtype, int64_t m, int64_t n, int64_t k, void* stream);
@@ -221,6 +234,58 @@ int fp4x_draft_head(const void* x, int64_t x_ld, const void* p, const void* s, i
 int fp4x_head_merge(const float* coarse, const float* exact, const int32_t* gidx, int64_t parts, int64_t m, int64_t c,
                     int64_t v, int32_t* idx_out, float* coarse_out, float* exact_out, int32_t* argmax_out,
                     void* stream);
+
+/* ---------------------------------------------------------------------------------------------------------
+ * Weight preparation on the GPU (replaces the reference's torch quantizers and dequantizers, K:138-357, and the
+ * lazy preparation of x/fp4patch.py:61-83, :206-214, :290-307).  Inputs are row-major [n, k] weights in fp32, bf16
+ * or f16 (FP4X_IN_*); outputs are the packed layouts listed at the top of this file.
+ * The reference evaluates `tensor / python_scalar` as an IEEE division on the CPU and as a multiplication by the
+ * fp32 reciprocal on CUDA devices, which can move a group scale by one ulp: FP4X_DIV_IEEE reproduces the
+ * reference run on the CPU, FP4X_DIV_RECIP the reference run on a CUDA device.
+ * --------------------------------------------------------------------------------------------------------- */
+#define FP4X_IN_F32 0
+#define FP4X_IN_BF16 1
+#define FP4X_IN_F16 2
+#define FP4X_DIV_IEEE 0
+#define FP4X_DIV_RECIP 1
+
+/* Replaces quantize_w8 (K:138-144): q int8 [n, k], s fp32 [n, k/64]. */
+int fp4x_quantize_w8(const void* w, int in_dtype, int64_t n, int64_t k, int8_t* q, float* s, int div_mode,
+                     void* stream);
+
+/* Replaces quantize_w6 with clip_search = 0 (K:179-202): lo [n, k/2], hi [n, k/4], s_f16 [n, k/32]. */
+int fp4x_quantize_w6(const void* w, int in_dtype, int64_t n, int64_t k, int qmax, uint8_t* lo, uint8_t* hi,
+                     void* s_f16, int div_mode, void* stream);
+
+/* Largest |w| over `count` weights into *amax_out (device fp32): the first pass of quantize_nv4 (K:286-288), whose
+ * global scale gs = max(amax / 6 / 448, 1e-30) is then formed on the host in double precision, as there. */
+int fp4x_amax(const void* w, int in_dtype, int64_t count, float* amax_out, void* stream);
+
+/* Replaces the packing pass of quantize_nv4 (K:289-300): p [n, k/2] (low nibble = even k), s e4m3 [n, k/16]. */
+int fp4x_quantize_nv4(const void* w, int in_dtype, int64_t n, int64_t k, double gs, uint8_t* p, uint8_t* s,
+                      int div_mode, void* stream);
+
+/* Replaces quantize_int2 with fp16 scales (K:330-351): p [n, k/4], s_f16 [n, k/group], group 16 or 32. */
+int fp4x_quantize_int2(const void* w, int in_dtype, int64_t n, int64_t k, int group, uint8_t* p, void* s_f16,
+                       int div_mode, void* stream);
+
+/* Replaces mx8_dequant (K:261-267): out fp32 [n, k] = e4m3 * 2^(s - 127). */
+int fp4x_mx8_dequant(const uint8_t* w8, const uint8_t* s, int64_t n, int64_t k, float* out, void* stream);
+
+/* Replaces dequant_nv4 (K:420-426): out fp32 [n, k] = e2m1 * e4m3 scale * gs. */
+int fp4x_dequant_nv4(const uint8_t* p, const uint8_t* s, double gs, int64_t n, int64_t k, float* out, void* stream);
+
+/* Replaces dequant_int2 (K:353-357): out fp32 [n, k] = (code - 1.5) * s. */
+int fp4x_dequant_int2(const uint8_t* p, const void* s_f16, int group, int64_t n, int64_t k, float* out, void* stream);
+
+/* Replaces the scale un-swizzle of the draft head's NVFP4 source (x/fp4patch.py:296): scales stored as 128-row x
+ * 4-column tiles, [n/128][kb/4][32][4][4], to row-major [n][kb] (row 128a + 32d + c, column 4b + e). */
+int fp4x_nv4_unswizzle_scales(const uint8_t* in, int64_t n, int64_t kb, uint8_t* out, void* stream);
+
+/* Replaces HCFused.interleave_up's row gather (K:513-517) for one plane of row_bytes bytes per row:
+ * out row (j * hc + s) * bj + t = in row s * (n / hc) + j * bj + t. */
+int fp4x_interleave_rows(const void* in, int64_t row_bytes, int64_t n, int64_t hc, int64_t bj, void* out,
+                         void* stream);
 
 #ifdef __cplusplus
 }

@@ -221,6 +221,36 @@ FP4X_DEV uint32_t pack_f16x2(float lo, float hi) {
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
   return d;
 }
+// packed fp32 pairs (sm_100 f32x2 arithmetic; each lane rounds exactly like the scalar instruction)
+FP4X_DEV uint64_t f32x2_from_bits(uint32_t lo, uint32_t hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(lo), "r"(hi));
+  return d;
+}
+FP4X_DEV uint64_t f32x2_splat(float v) { return f32x2_from_bits(__float_as_uint(v), __float_as_uint(v)); }
+FP4X_DEV uint64_t f32x2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+FP4X_DEV uint64_t f32x2_mul(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+FP4X_DEV uint64_t f32x2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+// the two fp32 lanes rounded to nearest-even bf16: low lane -> low half
+FP4X_DEV uint32_t f32x2_to_bf16x2(uint64_t v) {
+  uint32_t lo, hi, d;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "r"(hi), "r"(lo));
+  return d;
+}
+
 FP4X_DEV float bf16_bits_to_f32(uint32_t b16) { return __uint_as_float(b16 << 16); }
 FP4X_DEV float bf16_round(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
 FP4X_DEV float f16_bits_to_f32(uint32_t h) { return __half2float(__ushort_as_half((unsigned short)h)); }

@@ -8,8 +8,7 @@
 #include <vector>
 
 #include "fp4x_gemv.cuh"
-#include "fp4x_tc.cuh"
-#include "fp4x_tc_int2.cuh"
+#include "fp4x_launch.cuh"
 #include "fp4x_host.h"
 
 namespace fp4x {
@@ -81,7 +80,7 @@ cudaError_t ensure_smem_attr(const void* kernel, int bytes) {
 }
 
 // allow clusters of up to 16 CTAs for a kernel, once per (kernel, device)
-static cudaError_t ensure_nonportable_cluster(const void* kernel) {
+cudaError_t ensure_nonportable_cluster(const void* kernel) {
   static const void* done_k[256];
   static int done_d[256];
   static int n = 0;
@@ -132,7 +131,7 @@ static int encode_rows_uncached(CUtensorMap* tm, const void* ptr, int64_t rows, 
 }
 
 // [rows][row_bytes] u8 scale rows, box {box_bytes, 128 rows}, no swizzle (the tcgen05 kernels' scale tiles)
-static int encode_scale_box(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t row_bytes, int box_bytes) {
+int encode_scale_box(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t row_bytes, int box_bytes) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(FP4X_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
   const cuuint64_t gdim[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
@@ -147,7 +146,7 @@ static int encode_scale_box(CUtensorMap* tm, const void* ptr, int64_t rows, int6
 }
 
 // [rows][row_bytes] u8, box {box_bytes, box_rows}, 64-byte swizzle when box_bytes is 64 (the INT2 code tiles)
-static int encode_box(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t row_bytes, int box_bytes, int box_rows) {
+int encode_box(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t row_bytes, int box_bytes, int box_rows) {
   EncodeTiledFn enc = encode_fn();
   if (!enc) return fail(FP4X_ERR_CUDA, "cuTensorMapEncodeTiled is not available");
   const cuuint64_t gdim[2] = {(cuuint64_t)row_bytes, (cuuint64_t)rows};
@@ -162,7 +161,7 @@ static int encode_box(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t ro
   return FP4X_OK;
 }
 
-static int encode_rows(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t row_bytes, int inner) {
+int encode_rows(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t row_bytes, int inner) {
   struct Key {
     uintptr_t p;
     int64_t rows, rb;
@@ -199,16 +198,6 @@ static int encode_rows(CUtensorMap* tm, const void* ptr, int64_t rows, int64_t r
 // ------------------------------------------------------------------------------------------------------
 enum PlanMode { kStreamK = 0, kWholeTile = 1 };
 
-struct Plan {
-  int NT, MP;
-  int KPW, KP, KC, NCH, CPP, RT, NS, SMAX, whole;
-  int BI0, BI1, NB0, SB, STG, off_p1, off_sc, XP;
-  int smem_x, smem_misc, smem_scr, smem_xraw, smem_comb, smem_red, smem_total;
-  int xdirect;  // 16-token plans: the raw activation panel stays in global memory
-  int cluster;
-  size_t ws_bytes;
-  int64_t counters;
-};
 
 static int round_up(int v, int a) { return (v + a - 1) / a * a; }
 
@@ -417,39 +406,6 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
 // ------------------------------------------------------------------------------------------------------
 // launch
 // ------------------------------------------------------------------------------------------------------
-template <int FMT, int NT, int EPI, int SHAPE>
-static int launch_s(const Plan& pl, const GemvArgs& a, int64_t batch, cudaStream_t st) {
-  const bool wide = (int64_t)pl.CPP * pl.KP * batch <= device_facts().sms;
-  auto kern = wide ? gemv_kernel_wide<FMT, NT, EPI, SHAPE> : gemv_kernel<FMT, NT, EPI, SHAPE>;
-  cudaError_t e = ensure_smem_attr((const void*)kern, pl.smem_total);
-  if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
-  if (pl.cluster > 1) {
-    if (pl.cluster > 8) {
-      e = ensure_nonportable_cluster((const void*)kern);
-      if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute(non-portable cluster)");
-    }
-    return check_launch(launch_pdl_cluster(kern, dim3(pl.CPP, pl.KP, (unsigned)batch), dim3(kThreads), pl.smem_total,
-                                           st, pl.cluster, a),
-                        "gemv cluster launch");
-  }
-  return check_launch(launch_pdl(kern, dim3(pl.CPP, pl.KP, (unsigned)batch), dim3(kThreads), pl.smem_total, st, a),
-                      "gemv launch");
-}
-
-template <int FMT, int NT, int EPI>
-static int launch_t(const Plan& pl, const GemvArgs& a, int64_t batch, cudaStream_t st) {
-  if (pl.BI0 == 128) {
-    if (pl.NB0 == 2) return launch_s<FMT, NT, EPI, SHAPE_128x2>(pl, a, batch, st);
-    return launch_s<FMT, NT, EPI, SHAPE_128x1>(pl, a, batch, st);
-  }
-  return launch_s<FMT, NT, EPI, SHAPE_64x1>(pl, a, batch, st);
-}
-
-template <int FMT, int EPI>
-static int launch_nt(const Plan& pl, const GemvArgs& a, int64_t batch, cudaStream_t st) {
-  return pl.NT == 1 ? launch_t<FMT, 1, EPI>(pl, a, batch, st) : launch_t<FMT, 2, EPI>(pl, a, batch, st);
-}
-
 static void fill_args(const Plan& pl, GemvArgs& a) {
   a.err = dev_error_ptr();
   a.KPW = pl.KPW; a.KP = pl.KP; a.KC = pl.KC; a.NCH = pl.NCH; a.CPP = pl.CPP; a.RT = pl.RT; a.NS = pl.NS;
@@ -495,170 +451,6 @@ static int check_rows(const void* p, int64_t row_bytes, const char* what) {
   if (!aligned(p, 16) || row_bytes % 16 != 0)
     return fail(FP4X_ERR_UNSUPPORTED, std::string(what) + " rows must be 16-byte aligned");
   return FP4X_OK;
-}
-
-template <int MT>
-static int launch_nv4_tc(const tc::Args& a, unsigned grid, int smem_total, void* stream) {
-  auto kern = tc::nv4_tc_kernel<MT>;
-  cudaError_t e = ensure_smem_attr((const void*)kern, smem_total);
-  if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
-  return check_launch(
-      launch_pdl(kern, dim3(grid), dim3(tc::nv_threads(MT)), (size_t)smem_total, (cudaStream_t)stream, a),
-      "nv4 tcgen05 launch");
-}
-
-// NVFP4 on tcgen05 block-scaled MMAs (fp4x_tc.cuh): M <= 8 tokens, at least 64 row blocks of 128, K a multiple
-// of 256.  Returns 1 when the shape is not covered (the caller then uses the register-decode kernel).
-static int run_nv4_tc(const void* x, int64_t x_stride, const void* wp, const void* sc, float gs, void* out,
-                      int64_t out_stride, int out_dtype, int64_t m, int64_t n, int64_t k, void* stream) {
-  const DeviceFacts& dv = device_facts();
-  if (m < 1 || m > tc::kMaxM || k % tc::kKC != 0 || k / tc::kKC > tc::kMaxSlabs || n < 64 * tc::kRows ||
-      n > (1 << 30))
-    return 1;
-  const int NB = (tc::kTerms * (int)m + 15) / 16 * 16;
-  if (4 * (k / 64) > tc::kTmemCols - tc::kColSFB || NB > tc::kColSFA) return 1;
-  if (!aligned(x, 16) || x_stride % 8 != 0 || x_stride < k || !aligned(wp, 16) || (k / 2) % 16 != 0) return 1;
-  const int64_t lds = k / 16;
-  if (lds % 16 != 0 || !aligned(sc, 16) || !out || out_stride < n) return 1;
-  int rc;
-  if ((rc = check_out_dtype(out_dtype))) return rc;
-  tc::Args a;
-  std::memset(&a, 0, sizeof(a));
-  const int b_bytes = (int)(k / 256) * NB * 128;
-  const int xraw = round_up((int)(m * k * 2), 1024);
-  const int sfb = round_up((int)(k / 64) * 512, 1024);  // B scales in tcgen05.cp groups, one per 64-k block
-  const int fixed = b_bytes + xraw + sfb + tc::kMiscBytes + 1024;
-  int ns = (dv.smem_optin - fixed) / tc::kStageBytes;
-  if (ns > tc::kMaxStages) ns = tc::kMaxStages;
-  if (ns > (int)(k / tc::kKC)) ns = (int)(k / tc::kKC);
-  if (ns < 2) return 1;
-  a.NS = ns;
-  a.smem_b = ns * tc::kStageBytes;          // multiple of 1024
-  a.smem_xraw = a.smem_b + b_bytes;
-  a.smem_sfb = a.smem_xraw + xraw;
-  a.smem_misc = a.smem_sfb + sfb;
-  const int smem_total = a.smem_misc + tc::kMiscBytes + 1024;
-  if ((rc = encode_rows(&a.tm, wp, n, k / 2, 128))) return rc;
-  if ((rc = encode_scale_box(&a.tms, sc, n, k / 16, 16))) return rc;
-  a.x = (const __nv_bfloat16*)x; a.x_stride = x_stride;
-  a.sc = (const uint8_t*)sc; a.lds = lds; a.scw = 16;
-  a.out = out; a.out_stride = out_stride; a.out_dtype = out_dtype; a.gs = gs;
-  a.M = (int)m; a.N = (int)n; a.K = (int)k; a.NB = NB;
-  a.err = dev_error_ptr();
-  const unsigned grid = (unsigned)((n + tc::kRows - 1) / tc::kRows);
-  switch (m) {
-    case 1: return launch_nv4_tc<1>(a, grid, smem_total, stream);
-    case 2: return launch_nv4_tc<2>(a, grid, smem_total, stream);
-    case 3: return launch_nv4_tc<3>(a, grid, smem_total, stream);
-    case 4: return launch_nv4_tc<4>(a, grid, smem_total, stream);
-    case 5: return launch_nv4_tc<5>(a, grid, smem_total, stream);
-    case 6: return launch_nv4_tc<6>(a, grid, smem_total, stream);
-    case 7: return launch_nv4_tc<7>(a, grid, smem_total, stream);
-    default: return launch_nv4_tc<8>(a, grid, smem_total, stream);
-  }
-}
-
-template <int MT>
-static int launch_mx8_tc(const tc::MxArgs& a, unsigned grid, int smem_total, void* stream) {
-  auto kern = tc::mx8_tc_kernel<MT>;
-  cudaError_t e = ensure_smem_attr((const void*)kern, smem_total);
-  if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
-  return check_launch(launch_pdl(kern, dim3(grid), dim3(tc::kThreads), (size_t)smem_total, (cudaStream_t)stream, a),
-                      "mx8 tcgen05 launch");
-}
-
-// MXFP8 on tcgen05 block-scaled MMAs (fp4x_tc.cuh): M <= 8 tokens, at least 64 row blocks of 128, K a multiple of
-// 512 up to 4096.  Returns 1 when the shape is not covered (the caller then uses the register-decode kernel).
-static int run_mx8_tc(const void* x, int64_t x_stride, const void* w, const void* sc, void* out, int64_t out_stride,
-                      int out_dtype, int64_t m, int64_t n, int64_t k, void* stream) {
-  const DeviceFacts& dv = device_facts();
-  if (m < 1 || m > tc::kMaxM || k % 512 != 0 || k / tc::kMxKC > tc::kMxMaxChunks || n < 64 * tc::kRows ||
-      n > (1 << 30))
-    return 1;
-  if (!aligned(x, 16) || x_stride % 8 != 0 || x_stride < k || !aligned(w, 16) || !aligned(sc, 16) || !out ||
-      out_stride < n)
-    return 1;
-  int rc;
-  if ((rc = check_out_dtype(out_dtype))) return rc;
-  const int NB = (tc::kMxTerms * (int)m + 15) / 16 * 16;
-  tc::MxArgs a;
-  std::memset(&a, 0, sizeof(a));
-  const int b_bytes = (int)(k / tc::kMxKC) * NB * 128;
-  const int xraw = round_up((int)(m * k * 2), 1024);
-  const int sfb = round_up((int)(k / tc::kMxKC) * 512, 1024);
-  const int sfa = round_up(tc::kRows * (int)(k / 32), 1024);
-  const int misc = 1024;
-  const int fixed = b_bytes + xraw + sfb + sfa + misc + 1024;
-  int ns = (dv.smem_optin - fixed) / tc::kStageA;
-  if (ns > tc::kMxMaxStages) ns = tc::kMxMaxStages;
-  if (ns > (int)(k / tc::kMxKC)) ns = (int)(k / tc::kMxKC);
-  if (ns < 2) return 1;
-  a.NS = ns;
-  a.smem_b = ns * tc::kStageA;
-  a.smem_xraw = a.smem_b + b_bytes;
-  a.smem_sfb = a.smem_xraw + xraw;
-  a.smem_sfa = a.smem_sfb + sfb;
-  a.smem_misc = a.smem_sfa + sfa;
-  const int smem_total = a.smem_misc + misc + 1024;
-  if ((rc = encode_rows(&a.tm, w, n, k, 128))) return rc;
-  if ((rc = encode_scale_box(&a.tms, sc, n, k / 32, (int)(k / 32)))) return rc;
-  a.x = (const __nv_bfloat16*)x; a.x_stride = x_stride;
-  a.out = out; a.out_stride = out_stride; a.out_dtype = out_dtype;
-  a.M = (int)m; a.N = (int)n; a.K = (int)k;
-  a.err = dev_error_ptr();
-  const unsigned grid = (unsigned)((n + tc::kRows - 1) / tc::kRows);
-  switch (m) {
-    case 1: return launch_mx8_tc<1>(a, grid, smem_total, stream);
-    case 2: return launch_mx8_tc<2>(a, grid, smem_total, stream);
-    case 3: return launch_mx8_tc<3>(a, grid, smem_total, stream);
-    case 4: return launch_mx8_tc<4>(a, grid, smem_total, stream);
-    case 5: return launch_mx8_tc<5>(a, grid, smem_total, stream);
-    case 6: return launch_mx8_tc<6>(a, grid, smem_total, stream);
-    case 7: return launch_mx8_tc<7>(a, grid, smem_total, stream);
-    default: return launch_mx8_tc<8>(a, grid, smem_total, stream);
-  }
-}
-
-// INT2 head logits on tcgen05 (fp4x_tc_int2.cuh): M <= 16 tokens, at least 32 row tiles of 128, groups of 16 or
-// 32, K a multiple of 256 with the B operand (K x 32 bytes) fitting beside the stages.  Returns 1 when the shape is
-// not covered (the caller then uses the register-decode kernel).
-static int run_int2_tc(const void* x, int64_t x_stride, const void* p, const void* s, int group, void* out,
-                       void* out_bf16, int64_t out_stride, int out_dtype, int64_t m, int64_t n, int64_t k,
-                       void* stream) {
-  const DeviceFacts& dv = device_facts();
-  if (m < 1 || m > tc::kI2MaxM || (group != 16 && group != 32) || k % tc::kI2KC != 0 || n < 32 * tc::kRows ||
-      n > (1 << 30))
-    return 1;
-  if (!aligned(x, 16) || x_stride % 8 != 0 || x_stride < k || !aligned(p, 16) || !aligned(s, 16) || !out ||
-      out_stride < n)
-    return 1;
-  int rc;
-  if ((rc = check_out_dtype(out_dtype))) return rc;
-  const int b_bytes = (int)(k / 64) * 2048;
-  const int misc = 1024;
-  const int fixed = b_bytes + misc + 1024;
-  int ns = (dv.smem_optin - fixed) / tc::kI2StageBytes;
-  if (ns > tc::kI2MaxStages) ns = tc::kI2MaxStages;
-  if (ns < 4) return 1;
-  tc::I2Args a;
-  std::memset(&a, 0, sizeof(a));
-  a.NS = ns;
-  a.smem_b = ns * tc::kI2StageBytes;  // multiple of 1024
-  a.smem_misc = a.smem_b + b_bytes;
-  const int smem_total = a.smem_misc + misc + 1024;
-  if ((rc = encode_box(&a.tm, p, n, k / 4, 64, tc::kRows))) return rc;
-  if ((rc = encode_box(&a.tms, s, n, 2 * k / group, 512 / group, tc::kRows))) return rc;
-  a.x = (const __nv_bfloat16*)x; a.x_stride = x_stride;
-  a.out = out; a.out_bf16 = out_bf16; a.out_stride = out_stride; a.out_dtype = out_dtype;
-  a.M = (int)m; a.N = (int)n; a.K = (int)k; a.group = group;
-  a.tiles = (int)((n + tc::kRows - 1) / tc::kRows);
-  a.err = dev_error_ptr();
-  const unsigned grid = (unsigned)std::min(a.tiles, dv.sms);
-  auto kern = tc::int2_tc_kernel;
-  cudaError_t e = ensure_smem_attr((const void*)kern, smem_total);
-  if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
-  return check_launch(launch_pdl(kern, dim3(grid), dim3(tc::kI2Threads), (size_t)smem_total, (cudaStream_t)stream, a),
-                      "int2 tcgen05 launch");
 }
 
 // shared path of the single-matrix GEMVs
@@ -740,6 +532,20 @@ __global__ void hc_gate_mean_kernel(const __nv_bfloat16* g, const __nv_bfloat16*
   }
 }
 
+// Test hook of the bounded waits: one CTA waits on an mbarrier that no thread arrives on, through the production
+// wait with a short limit; the wait gives up, records kDevWaitTimeout in the error word and the kernel returns.
+__global__ void expire_wait_kernel(int* err, uint64_t limit_ns) {
+  __shared__ __align__(8) uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(smem_u32(&bar), 1);
+    mbar_init_fence();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait_bounded(smem_u32(&bar), 0, err, limit_ns);
+}
+
+int reset_static_counters(cudaStream_t st);
+
 }  // namespace fp4x
 
 using namespace fp4x;
@@ -762,12 +568,25 @@ int fp4x_device_error(void* stream, int clear, int* code_out) {
   if (e != cudaSuccess) return fail(FP4X_ERR_CUDA, std::string("reading the device error word: ") + cudaGetErrorString(e));
   if (code_out) *code_out = v;
   if (clear && v) {
+    // a kernel that gave up may have left arrival counters mid-count: the library's own static counters are
+    // zeroed here (caller-owned counter arrays are the caller's to zero)
+    int rc = reset_static_counters((cudaStream_t)stream);
+    if (rc) return rc;
     const int zero = 0;
     e = cudaMemcpyToSymbolAsync(g_dev_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, (cudaStream_t)stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
     if (e != cudaSuccess) return fail(FP4X_ERR_CUDA, cudaGetErrorString(e));
   }
   return v ? fail(FP4X_ERR_DEVICE, "device error word = " + std::to_string(v)) : FP4X_OK;
+}
+
+int fp4x_test_expire_wait(int64_t limit_ns, void* stream) {
+  if (limit_ns < 1000 || limit_ns > 1000000000) return fail(FP4X_ERR_INVALID_ARG, "limit_ns must be in [1e3, 1e9]");
+  int* err = dev_error_ptr();
+  if (!err) return fail(FP4X_ERR_CUDA, "device error word not available");
+  expire_wait_kernel<<<1, 32, 0, (cudaStream_t)stream>>>(err, (uint64_t)limit_ns);
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return check_launch(cudaGetLastError(), "expire-wait test kernel");
 }
 
 int fp4x_gemv_query(int fmt, int64_t m, int64_t n, int64_t k, int64_t batch, int group, size_t* ws_bytes,
@@ -997,7 +816,29 @@ static int static_scratch(void** ws, int32_t** counters) {
   return FP4X_OK;
 }
 
+int reset_static_counters(cudaStream_t st) {
+  void* ws = nullptr;
+  int32_t* cnt = nullptr;
+  int rc = static_scratch(&ws, &cnt);
+  if (rc) return rc;
+  cudaError_t e = cudaMemsetAsync(cnt, 0, sizeof(int32_t) * kStaticCounters, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return fail(FP4X_ERR_CUDA, std::string("zeroing the static counters: ") + cudaGetErrorString(e));
+  return FP4X_OK;
+}
+
 }  // namespace fp4x
+
+extern "C" int fp4x_test_set_static_counter(int64_t index, int32_t value, void* stream) {
+  if (index < 0 || index >= kStaticCounters) return fail(FP4X_ERR_INVALID_ARG, "counter index out of range");
+  void* ws = nullptr;
+  int32_t* cnt = nullptr;
+  int rc = static_scratch(&ws, &cnt);
+  if (rc) return rc;
+  cudaError_t e = cudaMemcpyAsync(cnt + index, &value, sizeof(int32_t), cudaMemcpyHostToDevice, (cudaStream_t)stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize((cudaStream_t)stream);
+  return check_launch(e, "writing a static counter");
+}
 
 extern "C" int fp4x_mx8_linear_noalloc(const void* x, int64_t x_stride, const void* w, const void* s, void* out,
                                        int64_t out_stride, int out_dtype, int64_t m, int64_t n, int64_t k,

@@ -50,8 +50,8 @@ struct FmtGeom {
 
 __host__ __device__ constexpr FmtGeom fmt_geom(int fmt) {
   return fmt == FMT_MX8    ? FmtGeom{16, 1, 1, 0, 1, 1, 32, 4, 1, 64}
-         : fmt == FMT_W8   ? FmtGeom{16, 1, 1, 0, 1, 1, 16, 4, 1, 64}
-         : fmt == FMT_W6   ? FmtGeom{32, 1, 2, 1, 4, 1, 16, 8, 1, 256}
+         : fmt == FMT_W8   ? FmtGeom{16, 1, 1, 0, 1, 1, 16, 4, 0, 64}
+         : fmt == FMT_W6   ? FmtGeom{32, 1, 2, 1, 4, 1, 16, 8, 0, 256}
          : fmt == FMT_NV4  ? FmtGeom{32, 1, 2, 0, 1, 1, 16, 4, 1, 128}
          : fmt == FMT_BF16 ? FmtGeom{8, 2, 1, 0, 1, 0, 1, 16, 0, 32}
                            : FmtGeom{64, 1, 4, 0, 1, 1, 8, 16, 0, 256};  // INT2 (scale sd set at runtime)
@@ -536,13 +536,23 @@ FP4X_DEV void stage_mx8(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) {
   }
 }
 
-FP4X_DEV uint32_t w8_pair_lo(uint32_t w) { return hadd2(prmt(w ^ 0x80808080u, 0x64646464u, 0x4140u), 0xE480E480u); }
-FP4X_DEV uint32_t w8_pair_hi(uint32_t w) { return hadd2(prmt(w ^ 0x80808080u, 0x64646464u, 0x4342u), 0xE480E480u); }
+// W8 weights exactly as the reference forms them (K:126-130): bf16(f32(q) * s) per weight, s the fp32 group scale.
+// A byte b = q + 128 (the code with its sign bit flipped) placed in bits 8..15 of 1.0f gives f = 1 + b * 2^-15;
+// f - (1 + 2^-8) = q * 2^-15 exactly, and multiplying by s * 2^15 (exact) rounds once, to fp32(q * s).  The pair
+// is then rounded to bf16x2.  `u` holds four biased codes; `h` picks bytes (0, 1) or (2, 3).
+FP4X_DEV uint32_t w8_bf16_pair(uint32_t u, int h, uint64_t s2) {
+  const uint32_t f0 = prmt(u, 0x3F800000u, h ? 0x7624u : 0x7604u);
+  const uint32_t f1 = prmt(u, 0x3F800000u, h ? 0x7634u : 0x7614u);
+  const uint64_t kBias = 0xBF808000BF808000ull;  // (-(1 + 2^-8), -(1 + 2^-8))
+  return f32x2_to_bf16x2(f32x2_mul(f32x2_add(f32x2_from_bits(f0, f1), kBias), s2));
+}
 
-// W8: four chunks per 64-group G; steps 4G + h
+// W8: four chunks per 64-group G; steps 4G + h.  Weights decoded to the reference's bf16 values, bf16 MMAs on the
+// raw bf16 activations.
 template <int NT, int NCHK>
 FP4X_DEV void stage_w8(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) {
   constexpr int NG = NCHK / 4;
+  constexpr int NACC = 2;
   const int G0 = (b * c.CPB + c0) >> 2;
   uint32_t r[NG][8];
   uint32_t b0[4 * NG][NT], b1[4 * NG][NT];
@@ -559,21 +569,33 @@ FP4X_DEV void stage_w8(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) {
     slo[j] = __uint_as_float(lds32(c.sc + (c.rbase + c.g) * c.SB + 4 * (G0 + j)));
     shi[j] = __uint_as_float(lds32(c.sc + (c.rbase + c.g + 8) * c.SB + 4 * (G0 + j)));
   }
+  float accs[NACC][NT][4];
+  zero_accs<NT, NACC>(accs);
 #pragma unroll
   for (int j = 0; j < NG; ++j) {
-    float tmp[NT][4];
+    const uint64_t s2lo = f32x2_splat(slo[j] * 32768.f), s2hi = f32x2_splat(shi[j] * 32768.f);
 #pragma unroll
     for (int h = 0; h < 4; ++h) {
-      const uint32_t lo = r[j][2 * h], hi = r[j][2 * h + 1];  // rows g, g+8 of chunk 4j + h
-      const uint32_t A[4] = {w8_pair_lo(lo), w8_pair_lo(hi), w8_pair_hi(lo), w8_pair_hi(hi)};
-      mma_f16_acc<NT>(tmp, A, b0[4 * j + h], b1[4 * j + h], h == 0);
+      const uint32_t lo = r[j][2 * h] ^ 0x80808080u, hi = r[j][2 * h + 1] ^ 0x80808080u;  // rows g, g+8
+      const uint32_t A[4] = {w8_bf16_pair(lo, 0, s2lo), w8_bf16_pair(hi, 0, s2hi), w8_bf16_pair(lo, 1, s2lo),
+                             w8_bf16_pair(hi, 1, s2hi)};
+      mma_bf16_acc<NT>(accs[h % NACC], A, b0[4 * j + h], b1[4 * j + h]);
     }
-    fma_scaled<NT>(acc, tmp, slo[j], shi[j]);
   }
+  fold_accs<NT, NACC>(acc, accs);
+}
+
+// Two 6-bit codes of a W6 pair word (code c_lo in bits 0..5, c_hi in bits 16..21 over the constant 0x3F803F80) to
+// the reference's bf16((c - 32) * s) (K:160-170).  Each half moved to the top of a word is the fp32 value
+// 1 + c * 2^-7; (c - 32) * s = f * (128 s) - 160 s, where 128 s and 160 s are exact (s is an fp16 value) and the
+// result has at most 17 significant bits, so one fused multiply-add gives it exactly and the bf16 rounding is the
+// reference's single rounding.
+FP4X_DEV uint32_t w6_bf16_pair(uint32_t w, uint64_t s128, uint64_t s160n) {
+  return f32x2_to_bf16x2(f32x2_fma(f32x2_from_bits(w << 16, w & 0xFFFF0000u), s128, s160n));
 }
 
 FP4X_DEV uint32_t w6_lane(uint32_t lo_src, uint32_t hi_src) {
-  return (lo_src & 0x000F000Fu) | (hi_src & 0x00300030u) | 0x64006400u;
+  return (lo_src & 0x000F000Fu) | (hi_src & 0x00300030u) | 0x3F803F80u;
 }
 
 // W6: a chunk of the low-nibble plane is one 32-group G (thread: 8 k = 32G + 8tq + r); steps 2G + h.
@@ -581,46 +603,40 @@ FP4X_DEV uint32_t w6_lane(uint32_t lo_src, uint32_t hi_src) {
 // 32 scale bytes per row), NCHK 4 the one-box stage (256 k: 64-byte high-bit rows, 16 scale bytes).  Every
 // address of the stage is a per-thread base XOR a constant: the bases have the varying bits clear (1024-aligned
 // planes, whole rows), and the varying parts (chunk pair, group) sit in bits the thread's fixed parts leave free.
-template <int NT, int NCHK>
-FP4X_DEV void stage_w6(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) {
-  constexpr int BI1 = NCHK == 8 ? 128 : 64;
-  constexpr int SB = NCHK == 8 ? 32 : 16;
-  const uint32_t kNeg1056 = 0xE420E420u;
-  const int G0 = b * 8 + c0;
-  const uint32_t a0 = c.p0 + (uint32_t)b * (uint32_t)(kRB * 128) + c.lrow0 + 16u * (uint32_t)((c0 + c.lsel) ^ c.lswz);
-  uint32_t hb[2], sb[2];
+// W6 one-box range: four 32-groups starting at group G0 (low-nibble chunk pair address a0, high-bit and scale row
+// bases hb / sb already offset to G0).  All shared-memory loads of the range are issued before its arithmetic.
+template <int NT>
+FP4X_DEV void w6_groups4(const WarpCtx& c, uint32_t a0, const uint32_t (&hb)[2], const uint32_t (&sb)[2], int G0,
+                         float (&accs)[2][NT][4]) {
+  uint32_t r[2][4];
+  uint32_t hs[4][2];
+  uint32_t b0[8][NT], b1[8][NT];
+  uint32_t sw[2][2];
 #pragma unroll
-  for (int q = 0; q < 2; ++q) {
-    const int row = c.rbase + c.g + 8 * q;
-    hb[q] = c.p1 + swz((uint32_t)(row * BI1 + 8 * G0 + 2 * c.tq), BI1);
-    sb[q] = c.sc + (uint32_t)(row * SB + 2 * G0);
-  }
-  uint32_t r[NCHK / 2][4];
-  uint32_t hs[NCHK][2];
-  uint32_t b0[2 * NCHK][NT], b1[2 * NCHK][NT];
-  uint32_t sw[2][NCHK / 2];
+  for (int u = 0; u < 2; ++u) ldsm_x4(a0 ^ (32u * u), r[u][0], r[u][1], r[u][2], r[u][3]);
 #pragma unroll
-  for (int u = 0; u < NCHK / 2; ++u) ldsm_x4(a0 ^ (32u * u), r[u][0], r[u][1], r[u][2], r[u][3]);
-#pragma unroll
-  for (int gg = 0; gg < NCHK; ++gg)
+  for (int gg = 0; gg < 4; ++gg)
 #pragma unroll
     for (int q = 0; q < 2; ++q) hs[gg][q] = lds16(hb[q] ^ (8u * gg));
 #pragma unroll
-  for (int s = 0; s < 2 * NCHK; ++s) load_b<NT>(c, 2 * G0 + s, b0[s], b1[s]);
+  for (int s = 0; s < 8; ++s) load_b<NT>(c, 2 * G0 + s, b0[s], b1[s]);
 #pragma unroll
-  for (int i = 0; i < NCHK / 2; ++i) {
+  for (int i = 0; i < 2; ++i) {
     sw[0][i] = lds32(sb[0] + 4 * i);
     sw[1][i] = lds32(sb[1] + 4 * i);
   }
 #pragma unroll
-  for (int gg = 0; gg < NCHK; ++gg) {
+  for (int gg = 0; gg < 4; ++gg) {
     uint32_t L[2], Hs[2];
+    uint64_t s128[2], s160[2];
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       L[q] = r[gg >> 1][2 * (gg & 1) + q];
       Hs[q] = prmt(hs[gg][q], 0u, 0x4140u);
+      const float s = f16_bits_to_f32((sw[q][gg >> 1] >> (16 * (gg & 1))) & 0xffffu);
+      s128[q] = f32x2_splat(128.f * s);
+      s160[q] = f32x2_splat(-160.f * s);
     }
-    float tmp[NT][4];
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       uint32_t A[4];
@@ -634,15 +650,42 @@ FP4X_DEV void stage_w6(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) {
           lo = w6_lane(L[q] >> 8, Hs[q] << 2);    // r2, r6
           hi = w6_lane(L[q] >> 12, Hs[q] >> 2);   // r3, r7
         }
-        A[q] = hadd2(lo, kNeg1056);
-        A[2 + q] = hadd2(hi, kNeg1056);
+        A[q] = w6_bf16_pair(lo, s128[q], s160[q]);
+        A[2 + q] = w6_bf16_pair(hi, s128[q], s160[q]);
       }
-      mma_f16_acc<NT>(tmp, A, b0[2 * gg + h], b1[2 * gg + h], h == 0);
+      mma_bf16_acc<NT>(accs[h], A, b0[2 * gg + h], b1[2 * gg + h]);
     }
-    const float sl = f16_bits_to_f32((sw[0][gg >> 1] >> (16 * (gg & 1))) & 0xffffu);
-    const float sh = f16_bits_to_f32((sw[1][gg >> 1] >> (16 * (gg & 1))) & 0xffffu);
-    fma_scaled<NT>(acc, tmp, sl, sh);
   }
+}
+
+// W6: a chunk of the low-nibble plane is one 32-group G (thread: 8 k = 32G + 8tq + r); steps 2G + h.
+// W6 stages always use 128-byte low-nibble boxes; NCHK 8 is the two-box stage (512 k: 128-byte high-bit rows,
+// 32 scale bytes per row), NCHK 4 the one-box stage (256 k: 64-byte high-bit rows, 16 scale bytes).  Every
+// address of the stage is a per-thread base XOR a constant: the bases have the varying bits clear (1024-aligned
+// planes, whole rows), and the varying parts (chunk pair, group) sit in bits the thread's fixed parts leave free.
+// The two-box stage runs as two four-group halves, which bounds the registers a warp holds.
+template <int NT, int NCHK>
+FP4X_DEV void stage_w6(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) {
+  constexpr int BI1 = NCHK == 8 ? 128 : 64;
+  constexpr int SB = NCHK == 8 ? 32 : 16;
+  const int G0 = b * 8 + c0;
+  const uint32_t a0 = c.p0 + (uint32_t)b * (uint32_t)(kRB * 128) + c.lrow0 + 16u * (uint32_t)((c0 + c.lsel) ^ c.lswz);
+  uint32_t hb[2], sb[2];
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    const int row = c.rbase + c.g + 8 * q;
+    hb[q] = c.p1 + swz((uint32_t)(row * BI1 + 8 * G0 + 2 * c.tq), BI1);
+    sb[q] = c.sc + (uint32_t)(row * SB + 2 * G0);
+  }
+  float accs[2][NT][4];
+  zero_accs<NT, 2>(accs);
+#pragma unroll
+  for (int half = 0; half < NCHK / 4; ++half) {
+    const uint32_t hbh[2] = {hb[0] ^ (32u * half), hb[1] ^ (32u * half)};
+    const uint32_t sbh[2] = {sb[0] + 8u * half, sb[1] + 8u * half};
+    w6_groups4<NT>(c, a0 ^ (64u * half), hbh, sbh, G0 + 4 * half, accs);
+  }
+  fold_accs<NT, 2>(acc, accs);
 }
 
 // NVFP4: a chunk C is 32 k = two 16-groups (thread: k = 32C + 8tq + 4h + i, group 2C + tq/2); steps 2C + h.
@@ -979,6 +1022,10 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
   }
 
   // ---------------- consumer warps ----------------
+  // start of this CTA's work: a cluster non-leader writes into the leader's shared memory only within 1 s of it, and
+  // the leader waits 2 s from a later moment (its own wait), so no remote write can land after the leader gave up
+  // (the CTAs of a cluster start together)
+  const uint64_t t_start = A.cluster > 1 ? global_ns() : 0;
   const int g = lane >> 2, tq = lane & 3;
   const int wrow = warp & (kRW - 1), kg = warp / kRW;
   pdl_wait();
@@ -1046,6 +1093,13 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
       constexpr uint32_t kSlot = 32u * NT * 16u;  // one row warp: 32 lanes x NT float4
       const uint32_t red = smem_u32(base + A.smem_red) + (uint32_t)wrow * kSlot + (uint32_t)lane * NT * 16u;
       if (rank != 0) {
+        int late = lane == 0 ? (global_ns() - t_start > 1000000000ull) : 0;  // one decision for the warp
+        late = __shfl_sync(0xffffffffu, late, 0);
+        if (late) {  // too late: the leader may have stopped waiting
+          if (lane == 0) set_dev_error(A.err, kDevWaitTimeout);
+          ok = false;
+          return;
+        }
         const uint32_t dst = mapa_shared(red + (rank - 1) * kRW * kSlot, 0);
 #pragma unroll
         for (int t = 0; t < NT; ++t) st_cluster_v4(dst + 16u * t, acc[t][0], acc[t][1], acc[t][2], acc[t][3]);

@@ -1,0 +1,7 @@
+// Instantiations of the GEMV launcher (fp4x_launch.cuh) compiled in their own translation unit.
+#include "fp4x_launch.cuh"
+
+namespace fp4x {
+template int launch_nt<FMT_W8, EPI_HC_DOWN>(const Plan&, const GemvArgs&, int64_t, cudaStream_t);
+template int launch_nt<FMT_W8, EPI_HC_UP>(const Plan&, const GemvArgs&, int64_t, cudaStream_t);
+}  // namespace fp4x

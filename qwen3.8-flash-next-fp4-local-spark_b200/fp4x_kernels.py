@@ -335,8 +335,11 @@ class HCFused:
     @staticmethod
     def interleave_up(q, s, hc, bj):
         """Reorder up rows [HC*H, K] so that each BJ-column tile holds its HC stream rows contiguously
-        (K:513-517): new row (j*HC + s)*BJ + t = old row s*H + j*BJ + t."""
+        (K:513-517): new row (j*HC + s)*BJ + t = old row s*H + j*BJ + t.  CUDA tensors: one gather kernel per
+        plane (fp4x_interleave_rows)."""
         n = q.shape[0]
+        if q.is_cuda and s.is_cuda:
+            return _interleave_native(q, hc, bj), _interleave_native(s, hc, bj)
         h = n // hc
         perm = torch.arange(n, device=q.device).view(hc, h // bj, bj).transpose(0, 1).reshape(-1)
         return q.index_select(0, perm).contiguous(), s.index_select(0, perm).contiguous()
@@ -382,7 +385,7 @@ def _row_blocks(n, rows):
 
 
 @torch.no_grad()
-def quantize_w8(w):
+def _torch_quantize_w8(w):
     """Symmetric int8 per 64-group: s = max(amax, 1e-12) / 127, q = clamp(round(w / s), +-127) (K:138-144)."""
     n, k = w.shape
     q = torch.empty((n, k), dtype=torch.int8, device=w.device)
@@ -426,7 +429,7 @@ def _w6_scale_search(f, qmax, clip, weight=None):
 
 
 @torch.no_grad()
-def quantize_w6(w, qmax=31, clip_search=0):
+def _torch_quantize_w6(w, qmax=31, clip_search=0):
     """6-bit g32 (K:179-202): s = max(fp16(amax/qmax), 6.2e-5), codes = clamp(round(w/s), -qmax-1, qmax) + 32.
     Returns (L [N,K/2] u8, H [N,K/4] u8, S [N,K/32] f16)."""
     n, k = w.shape
@@ -486,7 +489,7 @@ def quantize_w6_awq(w, h, qmax=31, clip=0, alpha=-1.0):
 
 
 @torch.no_grad()
-def mx8_dequant(w8, s_u8, rows=2048):
+def _torch_mx8_dequant(w8, s_u8, rows=2048):
     """MXFP8 -> fp32 [N, K]: e4m3 * 2^(s - 127) (K:261-267)."""
     n, k = w8.shape
     codes = w8.view(torch.float8_e4m3fn) if w8.dtype == torch.uint8 else w8
@@ -514,7 +517,7 @@ def quantize_mx8(w):
 
 
 @torch.no_grad()
-def quantize_nv4(w, rows=2048):
+def _torch_quantize_nv4(w, rows=2048):
     """NVFP4 (K:277-300): gs = max(amax/6/448, 1e-30) (python float), block scale = e4m3(clamp(amax16/6/gs,
     2^-9, 448)), magnitudes by nearest e2m1 level with ties to the lower level.  Returns (P, S e4m3, gs)."""
     global _E2M1
@@ -540,7 +543,7 @@ def quantize_nv4(w, rows=2048):
 
 
 @torch.no_grad()
-def dequant_nv4(P, S, gs):
+def _torch_dequant_nv4(P, S, gs):
     """[N, K/2] e2m1 pairs + [N, K/16] e4m3 scales -> fp32 [N, K] = v * s * gs (K:420-426)."""
     lut = torch.tensor(_E2M1_VALUES + tuple(-v for v in _E2M1_VALUES), device=P.device)
     n = P.shape[0]
@@ -549,7 +552,7 @@ def dequant_nv4(P, S, gs):
 
 
 @torch.no_grad()
-def quantize_int2(weight, scale_fmt="fp16", group=16):
+def _torch_quantize_int2(weight, scale_fmt="fp16", group=16):
     """INT2 per group (K:330-351): s = max(amax, 1e-8)/1.5 (fp16, or e4m3 relative to an fp32 row scale),
     code = clamp(floor(w/s) + 2, 0, 3), value (code - 1.5) * s; 4 codes per byte at bit pairs ORDER.
     Returns (packed, s) for fp16 scales, (packed, s_e4m3, row_scale) for e4m3."""
@@ -578,10 +581,201 @@ def quantize_int2(weight, scale_fmt="fp16", group=16):
     return (packed, scales) if scale_fmt == "fp16" else (packed, scales, rowsc)
 
 
-def dequant_int2(packed, scales):
+def _torch_dequant_int2(packed, scales):
     """fp32 (code - 1.5) * s (K:353-357)."""
     n = packed.shape[0]
     k = packed.shape[1] * 4
     codes = torch.stack([(packed >> (2 * ORDER[j])) & 3 for j in range(4)], -1).view(n, k).float() - 1.5
     g = k // scales.shape[1]
     return (codes.view(n, k // g, g) * scales.float().unsqueeze(-1)).view(n, k)
+
+
+# ----------------------------------------------------------------------------------------------------------
+# weight preparation entry points: CUDA tensors run the native kernels (libfp4x.so, fp4x_prep.cu); CPU tensors
+# run the torch restatements above (there is no GPU to run on).  The packed bytes are the reference's: its
+# quantizers evaluate `tensor / scalar` as a multiplication by the fp32 reciprocal on CUDA devices and as a
+# division on the CPU, and the native kernels follow the device's rule by default (FP4X_PREP_DIV=ieee|recip
+# overrides it).
+# ----------------------------------------------------------------------------------------------------------
+
+def _prep_mode():
+    import os
+    v = os.environ.get("FP4X_PREP_DIV", "recip").lower()
+    if v not in ("ieee", "recip"):
+        raise ValueError("FP4X_PREP_DIV must be 'ieee' or 'recip'")
+    return N.DIV_IEEE if v == "ieee" else N.DIV_RECIP
+
+
+def _prep_input(w):
+    """(contiguous weights, input dtype code) for the native quantizers."""
+    codes = {torch.float32: N.IN_F32, torch.bfloat16: N.IN_BF16, torch.float16: N.IN_F16}
+    if w.dtype not in codes:
+        w = w.float()
+    w = w.contiguous()
+    return w, codes[w.dtype]
+
+
+def _interleave_native(t, hc, bj):
+    t = t.contiguous()
+    n = t.shape[0]
+    out = torch.empty_like(t)
+    row_bytes = t.numel() * t.element_size() // n
+    N.call("fp4x_interleave_rows", N.ptr(t), row_bytes, n, hc, bj, N.ptr(out), N.stream_of(t))
+    return out
+
+
+@torch.no_grad()
+def quantize_w8(w, div_mode=None):
+    """Symmetric int8 per 64-group: s = max(amax, 1e-12) / 127, q = clamp(round(w / s), +-127) (K:138-144).
+    Returns (q int8 [N, K], s fp32 [N, K/64])."""
+    if not w.is_cuda:
+        return _torch_quantize_w8(w)
+    n, k = w.shape
+    wc, code = _prep_input(w)
+    q = torch.empty((n, k), dtype=torch.int8, device=w.device)
+    s = torch.empty((n, k // 64), dtype=torch.float32, device=w.device)
+    N.call("fp4x_quantize_w8", N.ptr(wc), code, n, k, N.ptr(q), N.ptr(s),
+           _prep_mode() if div_mode is None else div_mode, N.stream_of(wc))
+    return q, s
+
+
+@torch.no_grad()
+def quantize_w6(w, qmax=31, clip_search=0, div_mode=None):
+    """6-bit g32 (K:179-202): s = max(fp16(amax/qmax), 6.2e-5), codes = clamp(round(w/s), -qmax-1, qmax) + 32.
+    Returns (L [N,K/2] u8, H [N,K/4] u8, S [N,K/32] f16).  The clip search (clip_search > 0, a quality probe of the
+    reference whose choice depends on the summation order of torch's reductions) stays in torch."""
+    if not w.is_cuda or clip_search:
+        return _torch_quantize_w6(w, qmax, clip_search)
+    n, k = w.shape
+    wc, code = _prep_input(w)
+    L = torch.empty((n, k // 2), dtype=torch.uint8, device=w.device)
+    H = torch.empty((n, k // 4), dtype=torch.uint8, device=w.device)
+    S = torch.empty((n, k // 32), dtype=torch.float16, device=w.device)
+    N.call("fp4x_quantize_w6", N.ptr(wc), code, n, k, int(qmax), N.ptr(L), N.ptr(H), N.ptr(S),
+           _prep_mode() if div_mode is None else div_mode, N.stream_of(wc))
+    return L, H, S
+
+
+@torch.no_grad()
+def quantize_nv4(w, rows=2048, div_mode=None):
+    """NVFP4 (K:277-300): gs = max(amax/6/448, 1e-30) (python float), block scale = e4m3(clamp(amax16/6/gs,
+    2^-9, 448)), magnitudes by nearest e2m1 level with ties to the lower level.  Returns (P, S e4m3, gs)."""
+    if not w.is_cuda:
+        return _torch_quantize_nv4(w, rows)
+    n, k = w.shape
+    wc, code = _prep_input(w)
+    amax = torch.empty((1,), dtype=torch.float32, device=w.device)
+    N.call("fp4x_amax", N.ptr(wc), code, wc.numel(), N.ptr(amax), N.stream_of(wc))
+    gs = max(float(amax.item()) / 6.0 / 448.0, 1e-30)  # a host sync, as the reference's .item()
+    P = torch.empty((n, k // 2), dtype=torch.uint8, device=w.device)
+    S = torch.empty((n, k // 16), dtype=torch.float8_e4m3fn, device=w.device)
+    N.call("fp4x_quantize_nv4", N.ptr(wc), code, n, k, gs, N.ptr(P), N.ptr(S),
+           _prep_mode() if div_mode is None else div_mode, N.stream_of(wc))
+    return P, S, gs
+
+
+@torch.no_grad()
+def quantize_int2(weight, scale_fmt="fp16", group=16, div_mode=None):
+    """INT2 per group (K:330-351): s = max(amax, 1e-8)/1.5 (fp16, or e4m3 relative to an fp32 row scale),
+    code = clamp(floor(w/s) + 2, 0, 3), value (code - 1.5) * s; 4 codes per byte at bit pairs ORDER.
+    Returns (packed, s) for fp16 scales, (packed, s_e4m3, row_scale) for e4m3 (torch only: the reference does
+    not ship that variant)."""
+    if not weight.is_cuda or scale_fmt != "fp16":
+        return _torch_quantize_int2(weight, scale_fmt, group)
+    n, k = weight.shape
+    wc, code = _prep_input(weight)
+    P = torch.empty((n, k // 4), dtype=torch.uint8, device=weight.device)
+    S = torch.empty((n, k // group), dtype=torch.float16, device=weight.device)
+    N.call("fp4x_quantize_int2", N.ptr(wc), code, n, k, group, N.ptr(P), N.ptr(S),
+           _prep_mode() if div_mode is None else div_mode, N.stream_of(wc))
+    return P, S
+
+
+@torch.no_grad()
+def mx8_dequant(w8, s_u8, rows=2048):
+    """MXFP8 -> fp32 [N, K]: e4m3 * 2^(s - 127) (K:261-267)."""
+    if not w8.is_cuda:
+        return _torch_mx8_dequant(w8, s_u8, rows)
+    n, k = w8.shape
+    w, s = _rows(_u8(w8)), _rows(_u8(s_u8))
+    out = torch.empty((n, k), dtype=torch.float32, device=w8.device)
+    N.call("fp4x_mx8_dequant", N.ptr(w), N.ptr(s), n, k, N.ptr(out), N.stream_of(w))
+    return out
+
+
+@torch.no_grad()
+def dequant_nv4(P, S, gs):
+    """[N, K/2] e2m1 pairs + [N, K/16] e4m3 scales -> fp32 [N, K] = v * s * gs (K:420-426)."""
+    if not P.is_cuda:
+        return _torch_dequant_nv4(P, S, gs)
+    n, k = P.shape[0], P.shape[1] * 2
+    out = torch.empty((n, k), dtype=torch.float32, device=P.device)
+    N.call("fp4x_dequant_nv4", N.ptr(_rows(P)), N.ptr(_rows(_u8(S))), float(gs), n, k, N.ptr(out), N.stream_of(P))
+    return out
+
+
+@torch.no_grad()
+def dequant_int2(packed, scales):
+    """fp32 (code - 1.5) * s (K:353-357)."""
+    if not packed.is_cuda or scales.dtype != torch.float16:
+        return _torch_dequant_int2(packed, scales)
+    n, k = packed.shape[0], packed.shape[1] * 4
+    group = k // scales.shape[1]
+    out = torch.empty((n, k), dtype=torch.float32, device=packed.device)
+    N.call("fp4x_dequant_int2", N.ptr(_rows(packed)), N.ptr(_rows(scales)), group, n, k, N.ptr(out),
+           N.stream_of(packed))
+    return out
+
+
+@torch.no_grad()
+def nv4_unswizzle_scales(sc):
+    """NVFP4 scales stored as swizzled 128-row x 4-column tiles -> row-major [N, K/16] (the preparation of the
+    draft head's source scales, x/fp4patch.py:296: reshape(n//128, kb//4, 32, 4, 4).transpose(1, 3))."""
+    n, kb = sc.shape
+    u = _u8(sc)
+    if not sc.is_cuda:
+        return u.reshape(n // 128, kb // 4, 32, 4, 4).transpose(1, 3).reshape(n, kb).view(sc.dtype)
+    u = _rows(u)
+    out = torch.empty((n, kb), dtype=torch.uint8, device=sc.device)
+    N.call("fp4x_nv4_unswizzle_scales", N.ptr(u), n, kb, N.ptr(out), N.stream_of(u))
+    return out.view(sc.dtype)
+
+
+class PackedCache:
+    """Packed weights kept on disk between runs (safetensors files, one per weight), so a restarted server skips
+    the quantization pass that the reference repeats lazily on every start (x/fp4patch.py:61-83, :206-214).
+
+    get(name, build) returns the tuple `build()` produces (tensors, plus python floats such as the NVFP4 global
+    scale), loading it from `<dir>/<name>.safetensors` when present and writing it there otherwise."""
+
+    def __init__(self, directory, device="cuda"):
+        import os
+        self.dir = directory
+        self.device = torch.device(device)
+        os.makedirs(directory, exist_ok=True)
+
+    def path(self, name):
+        import os
+        safe = "".join(c if c.isalnum() or c in "._-" else "_" for c in name)
+        return os.path.join(self.dir, safe + ".safetensors")
+
+    def get(self, name, build):
+        import os
+        from safetensors.torch import load_file, save_file
+        p = self.path(name)
+        if os.path.exists(p):
+            d = load_file(p, device=str(self.device))
+            items = []
+            for i in range(len(d)):
+                t = d[f"{i}"]
+                items.append(float(t.item()) if t.dtype == torch.float64 and t.dim() == 0 else t)
+            return tuple(items)
+        out = build()
+        tensors = {}
+        for i, v in enumerate(out):
+            tensors[f"{i}"] = (v.detach().contiguous().cpu() if torch.is_tensor(v)
+                               else torch.tensor(float(v), dtype=torch.float64))
+        tmp = p + ".tmp"
+        save_file(tensors, tmp)
+        os.replace(tmp, p)
+        return out

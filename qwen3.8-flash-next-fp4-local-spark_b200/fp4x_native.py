@@ -3,8 +3,9 @@
 torch provides device memory and the current stream; every call passes raw pointers, integer sizes and the
 stream handle to the C ABI.  There is no fallback: if the library is missing or a call fails, a Python exception
 is raised.  Scratch memory for split reductions is allocated here through torch's caching allocator (so it is
-safe under CUDA-graph capture); the arrival counters live in one persistent zeroed int32 buffer per device that
-the kernels leave zeroed after every call.
+safe under CUDA-graph capture).  The arrival counters live in persistent zeroed int32 buffers that the kernels
+leave zeroed after every call, one per (device, stream): calls issued on different streams may run at the same time
+(vLLM overlaps decode linears on two streams) and never share a counter.
 """
 from __future__ import annotations
 
@@ -20,6 +21,8 @@ LIB_PATH = os.environ.get("FP4X_LIB", os.path.join(_HERE, "libfp4x.so"))
 OK = 0
 ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_CUDA, ERR_DEVICE = -1, -2, -3, -4, -5
 FMT_MX8, FMT_W8, FMT_W6, FMT_NV4, FMT_BF16, FMT_INT2 = range(6)
+IN_F32, IN_BF16, IN_F16 = range(3)
+DIV_IEEE, DIV_RECIP = 0, 1
 _DTYPES = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 
 _p = ctypes.c_void_p
@@ -40,6 +43,8 @@ _SIGS = {
     "fp4x_last_error_message": ([], ctypes.c_char_p),
     "fp4x_launch_count": ([], _i64),
     "fp4x_device_error": ([_p, _i32, ctypes.POINTER(ctypes.c_int)], _i32),
+    "fp4x_test_expire_wait": ([_i64, _p], _i32),
+    "fp4x_test_set_static_counter": ([_i64, ctypes.c_int32, _p], _i32),
     "fp4x_gemv_query": ([_i32, _i64, _i64, _i64, _i64, _i32, ctypes.POINTER(_sz), ctypes.POINTER(_i64)], _i32),
     "fp4x_plan_describe": ([_i32, _i64, _i64, _i64, _i64, _i32, _i32, ctypes.c_char_p, _sz], _i32),
     "fp4x_mx8_linear": ([_p, _i64, _p, _p, _p, _i64, _i32, _i64, _i64, _i64, _p, _sz, _p, _i64, _p], _i32),
@@ -68,6 +73,16 @@ _SIGS = {
     "fp4x_draft_head": ([_p, _i64, _p, _p, _i32, _p, _p, _f32, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64,
                          _p, _sz, _p, _i64, _p], _i32),
     "fp4x_head_merge": ([_p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p], _i32),
+    "fp4x_quantize_w8": ([_p, _i32, _i64, _i64, _p, _p, _i32, _p], _i32),
+    "fp4x_quantize_w6": ([_p, _i32, _i64, _i64, _i32, _p, _p, _p, _i32, _p], _i32),
+    "fp4x_amax": ([_p, _i32, _i64, _p, _p], _i32),
+    "fp4x_quantize_nv4": ([_p, _i32, _i64, _i64, ctypes.c_double, _p, _p, _i32, _p], _i32),
+    "fp4x_quantize_int2": ([_p, _i32, _i64, _i64, _i32, _p, _p, _i32, _p], _i32),
+    "fp4x_mx8_dequant": ([_p, _p, _i64, _i64, _p, _p], _i32),
+    "fp4x_dequant_nv4": ([_p, _p, ctypes.c_double, _i64, _i64, _p, _p], _i32),
+    "fp4x_dequant_int2": ([_p, _p, _i32, _i64, _i64, _p, _p], _i32),
+    "fp4x_nv4_unswizzle_scales": ([_p, _i64, _i64, _p, _p], _i32),
+    "fp4x_interleave_rows": ([_p, _i64, _i64, _i64, _i64, _p, _p], _i32),
 }
 
 _lib = None
@@ -129,21 +144,68 @@ def dtype_code(dt):
 # ---------------------------------------------------------------------------------------------------------
 # scratch
 # ---------------------------------------------------------------------------------------------------------
-_counters = {}
+_counters = {}   # (device index, stream handle) -> zeroed int32 counter buffer
+_spares = {}     # device index -> zeroed buffers kept for streams first seen under CUDA-graph capture
+_retired = []    # buffers replaced by larger ones (captured graphs may still point at them)
+COUNTER_WORDS = 1 << 16
+SPARES_PER_DEVICE = 4
+
+
+def _device_index(device):
+    d = torch.device(device) if device is not None else torch.device("cuda")
+    return d.index if d.index is not None else torch.cuda.current_device()
 
 
 def counters(device, n):
-    """Persistent zeroed int32 arrival counters on `device` (grown on demand, never during capture)."""
-    key = torch.device(device).index if torch.device(device).index is not None else torch.cuda.current_device()
+    """Persistent zeroed int32 arrival counters for the current stream of `device`.
+
+    Each (device, stream) pair has its own buffer, so kernels launched on different streams never share a counter.
+    A stream that is first seen while it is being captured takes one of the zeroed spare buffers allocated with the
+    device's first buffer; when none is left, the buffer is allocated inside the capture (from the graph's memory
+    pool, zeroed by a memset node that every replay runs).  Buffers are never freed (a captured graph may hold their
+    address)."""
+    dev = _device_index(device)
+    key = (dev, torch.cuda.current_stream(dev).cuda_stream)
     buf = _counters.get(key)
-    if buf is None or buf.numel() < n:
-        if torch.cuda.is_current_stream_capturing():
-            raise RuntimeError("fp4x counter buffer must be sized before CUDA-graph capture "
-                               "(run the call once eagerly first)")
-        size = max(n, 1 << 16, 0 if buf is None else 2 * buf.numel())
-        buf = torch.zeros(size, dtype=torch.int32, device=torch.device("cuda", key))
+    if buf is not None and buf.numel() >= n:
+        return buf
+    if torch.cuda.is_current_stream_capturing():
+        spares = _spares.get(dev, [])
+        for i, sp in enumerate(spares):
+            if sp.numel() >= n:
+                _counters[key] = spares.pop(i)
+                return _counters[key]
+        if buf is not None:
+            _retired.append(buf)
+        buf = torch.zeros(max(n, COUNTER_WORDS), dtype=torch.int32, device=torch.device("cuda", dev))
         _counters[key] = buf
+        return buf
+    size = max(n, COUNTER_WORDS, 0 if buf is None else 2 * buf.numel())
+    if buf is not None:
+        _retired.append(buf)
+    buf = torch.zeros(size, dtype=torch.int32, device=torch.device("cuda", dev))
+    _counters[key] = buf
+    spares = _spares.setdefault(dev, [])
+    while len(spares) < SPARES_PER_DEVICE:
+        spares.append(torch.zeros(max(size, COUNTER_WORDS), dtype=torch.int32, device=torch.device("cuda", dev)))
     return buf
+
+
+def counter_buffers(device=None):
+    """Every counter buffer of `device` (all devices when None), in use, spare or retired."""
+    out = list(_counters.items())
+    bufs = [b for (d, _), b in out if device is None or d == _device_index(device)]
+    for d, sp in _spares.items():
+        if device is None or d == _device_index(device):
+            bufs.extend(sp)
+    bufs.extend(b for b in _retired if device is None or b.device.index == _device_index(device))
+    return bufs
+
+
+def reset_counters(device=None):
+    """Zero every counter buffer of `device` (after a bounded device wait gave up, some may be left non-zero)."""
+    for b in counter_buffers(device):
+        b.zero_()
 
 
 def query(fmt, m, n, k, batch=1, group=16):
@@ -192,7 +254,16 @@ def launch_count():
 
 
 def device_error(clear=True, device=None):
+    """The device error word of `device` (0: no bounded wait gave up since the last clear).  With `clear`, a non-zero
+    word is reset together with every arrival counter of the device (the library's static counters included), since
+    a kernel that gave up may have left its counters mid-count."""
     code = ctypes.c_int(0)
-    rc = lib().fp4x_device_error(stream_of(None if device is None else torch.empty(0, device=device)),
-                                 1 if clear else 0, ctypes.byref(code))
-    return code.value if rc in (OK, ERR_DEVICE) else rc
+    st = stream_of(None if device is None else torch.empty(0, device=device))
+    rc = lib().fp4x_device_error(st, 1 if clear else 0, ctypes.byref(code))
+    if rc not in (OK, ERR_DEVICE):
+        return rc
+    if clear and code.value:
+        torch.cuda.synchronize(device)
+        reset_counters(device)
+        torch.cuda.synchronize(device)
+    return code.value

@@ -108,8 +108,10 @@ class ShardedFastHead:
         self.P, self.S, self.w8, self.s8 = F._rows(P), F._rows(S), F._rows(F._u8(w8)), F._rows(F._u8(s8))
         self.V, self.C, self.rank, self.world, self.group = V, C, rank, world, group
 
-    def local(self, h):
-        """The shard's own candidates: (coarse, exact, global ids) [M, C] each, and the coarse bf16 logits."""
+    def local(self, h, argmax=False):
+        """The shard's own candidates: (coarse, exact, global ids) [M, C] each, and the coarse bf16 logits; with
+        `argmax`, also the global id of the largest exact value among the shard's candidates ([M] int32), which on a
+        single shard is the head's answer (no merge needed)."""
         h = F._act(h)
         m, k = h.shape
         rows = self.stop - self.start
@@ -118,11 +120,15 @@ class ShardedFastHead:
         idx = torch.empty((m, self.C), dtype=torch.int32, device=h.device)
         exact = torch.empty((m, self.C), dtype=torch.float32, device=h.device)
         coarse = torch.empty((m, self.C), dtype=torch.float32, device=h.device)
+        amax = torch.empty((m,), dtype=torch.int32, device=h.device) if argmax else None
         ws, cnt = N.head_scratch(m, rows, k, self.C, group, h.device)
         N.call("fp4x_fast_head", N.ptr(h), h.stride(0), N.ptr(self.P), N.ptr(self.S), group, N.ptr(self.w8),
                N.ptr(self.s8), m, rows, k, self.C, N.ptr(full), full.stride(0), N.ptr(idx), N.ptr(exact),
-               N.ptr(coarse), None, N.ptr(ws), ws.numel(), N.ptr(cnt), cnt.numel(), N.stream_of(h))
-        return coarse, exact, idx + self.start, full
+               N.ptr(coarse), N.ptr(amax), N.ptr(ws), ws.numel(), N.ptr(cnt), cnt.numel(), N.stream_of(h))
+        gidx = idx + self.start if self.start else idx
+        if argmax:
+            return coarse, exact, gidx, full, (amax + self.start if self.start else amax)
+        return coarse, exact, gidx, full
 
     def __call__(self, h):
         coarse, exact, gidx, _ = self.local(h)

@@ -80,3 +80,43 @@ def test_interleave_up_matches_reference():
     s = torch.arange(128).view(-1, 1).float()
     _, so = F.HCFused.interleave_up(q, s, 4, 8)
     assert np.array_equal(so[:, 0].long().numpy(), FIX["ileave_perm"])
+
+
+def test_packed_cache_roundtrip_cpu(tmp_path):
+    """PackedCache writes the packed tuple once (safetensors) and loads it back bit for bit, python floats included."""
+    w = torch.randn(64, 512, generator=torch.Generator().manual_seed(2)) * 0.02
+    cache = F.PackedCache(str(tmp_path), "cpu")
+    built = cache.get("blk.0/nv4", lambda: F.quantize_nv4(w))
+    assert (tmp_path / "blk.0_nv4.safetensors").exists()
+    loaded = cache.get("blk.0/nv4", lambda: pytest.fail("must load from disk"))
+    assert isinstance(loaded[2], float) and loaded[2] == built[2]
+    assert torch.equal(loaded[0], built[0]) and torch.equal(loaded[1].view(torch.uint8), built[1].view(torch.uint8))
+
+
+def test_unswizzle_scales_cpu_matches_index_formula():
+    n, kb = 256, 32
+    sc = torch.arange(n * kb, dtype=torch.int64).remainder(251).to(torch.uint8).view(n, kb)
+    out = F.nv4_unswizzle_scales(sc)
+    flat = sc.reshape(-1)
+    for row in (0, 1, 31, 32, 127, 128, 200, 255):
+        for col in (0, 3, 4, 17, 31):
+            a, d, c, b, e = row // 128, (row // 32) % 4, row % 32, col // 4, col % 4
+            assert out[row, col] == flat[(((a * (kb // 4) + b) * 32 + c) * 4 + d) * 4 + e]
+
+
+def test_eager_baseline_restatement_matches_oracle():
+    """The CPU baseline's torch eager dequantizers (oracle/fp4x_eager.py) equal the numpy oracle's weights."""
+    import sys, os
+    sys.path.insert(0, os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "oracle"))
+    import fp4x_eager as E
+    w = torch.randn(64, 512, generator=torch.Generator().manual_seed(4)) * 0.02
+    c, s = F.quantize_mx8(w)
+    assert np.array_equal(E.mx8_dequant(c, s).numpy(), O.mx8_dequant(c.view(torch.uint8).numpy(), s.numpy()))
+    q, s = F.quantize_w8(w)
+    assert np.array_equal(E.w8_dequant(q, s).numpy(), O.w8_weights(q.numpy(), s.numpy()))
+    L, H, S = F.quantize_w6(w)
+    assert np.array_equal(E.w6_dequant(L, H, S).numpy(), O.w6_weights(L.numpy(), H.numpy(), S.numpy()))
+    P, S, gs = F.quantize_nv4(w)
+    assert np.array_equal(E.nv4_dequant(P, S).numpy(), O.nv4_weights(P.numpy(), S.view(torch.uint8).numpy()))
+    P, S = F.quantize_int2(w)
+    assert np.array_equal(E.int2_dequant(P, S).numpy(), O.int2_weights(P.numpy(), S.numpy()))

@@ -153,3 +153,47 @@ def test_fix_full_restores_unselected_candidates():
     want = coarse.to(torch.bfloat16)
     want.scatter_(1, idx.long(), exm.to(torch.bfloat16))
     assert torch.equal(full, want)
+
+
+def _lost_rank_worker(rank, world, port, q):
+    """Rank 1 joins the group and leaves before the candidate exchange; rank 0 must get an error from its all-gather
+    within the group's short timeout instead of waiting for ever."""
+    import datetime
+    import time
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=5))
+    if rank == 1:
+        q.put((rank, "left"))
+        q.close()
+        q.join_thread()
+        os._exit(0)  # between steps, with nothing in flight
+    m, c = 3, 16
+    co, ex = torch.zeros(m, c), torch.zeros(m, c)
+    gi = torch.zeros(m, c, dtype=torch.int32)
+    t0 = time.time()
+    try:
+        gather_candidates(co, ex, gi)
+        q.put((rank, "no error"))
+    except Exception as e:  # noqa: BLE001 - any failure of the collective is the expected outcome
+        q.put((rank, f"raised after {time.time() - t0:.1f} s: {type(e).__name__}"))
+    q.close()
+    q.join_thread()
+    os._exit(0)
+
+
+def test_gather_candidates_raises_when_a_rank_is_gone():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_lost_rank_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+        if p.is_alive():
+            p.kill()
+    assert results[1] == "left"
+    assert results[0].startswith("raised after"), results[0]
+    assert float(results[0].split()[2]) < 60.0

@@ -1,15 +1,17 @@
-"""fp4x_mx8_linear_noalloc (static library scratch, no caller workspace) against fp4x_mx8_linear (caller scratch
-from torch), called through the C ABI.  Kept in its own file that is collected last.
+"""fp4x_mx8_linear_noalloc (static library scratch, no caller workspace), called through the C ABI, against the CPU
+oracle and against fp4x_mx8_linear (caller scratch from torch).  Kept in its own file that is collected last.
 
-Tolerance: max |a - b| / max |b| < 1e-2 (the dense GEMV bound); both calls in a row are checked.
+Tolerances (max |a - b| / max |b|): fp32 output against the oracle's exact sums 5e-5 (fp32 summation only, as for
+every dense GEMV); bf16 output against the scratch-taking entry 1e-2.  Two calls in a row are checked, since the
+static scratch keeps what the previous call left in it.
 """
-import ctypes
-
+import numpy as np
 import pytest
 import torch
 
 import fp4x_kernels as F
 import fp4x_native as N
+from oracle import fp4x_oracle as O
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -30,31 +32,60 @@ def reference_call(x, w8, s):
     return out
 
 
-def noalloc_call(x, w8, s, n=None):
+def noalloc_call(x, w8, s, n=None, dtype=torch.bfloat16):
     m, k = x.shape
     n = w8.shape[0] if n is None else n
-    out = torch.empty(m, w8.shape[0], dtype=torch.bfloat16, device=DEV)
-    rc = N.lib().fp4x_mx8_linear_noalloc(N.ptr(x), x.stride(0), N.ptr(w8), N.ptr(s), N.ptr(out), out.stride(0), 0,
-                                         m, n, k, N.stream_of(x))
+    out = torch.empty(m, w8.shape[0], dtype=dtype, device=DEV)
+    rc = N.lib().fp4x_mx8_linear_noalloc(N.ptr(x), x.stride(0), N.ptr(w8), N.ptr(s), N.ptr(out), out.stride(0),
+                                         N.dtype_code(dtype), m, n, k, N.stream_of(x))
     return rc, out
+
+
+def case(m, n, k):
+    g = torch.Generator().manual_seed(n + k + m)
+    w = torch.randn(n, k, generator=g) * 0.02
+    codes, sc = F.quantize_mx8(w)
+    x = torch.randn(m, k, generator=g).to(torch.bfloat16)
+    oracle = O.mx8_linear(x.float().numpy(), codes.view(torch.uint8).numpy(), sc.numpy())
+    return x.to(DEV), codes.view(torch.uint8).contiguous().to(DEV), sc.contiguous().to(DEV), oracle
 
 
 @pytest.mark.parametrize("m", [1, 3, 16])
 @pytest.mark.parametrize("n,k", [(16384, 2560), (2560, 2560), (100, 512)])
-def test_noalloc_matches_scratch_entry(m, n, k):
-    g = torch.Generator().manual_seed(n + k + m)
-    w = (torch.randn(n, k, generator=g) * 0.02).to(DEV)
-    codes, sc = F.quantize_mx8(w)
-    w8 = codes.view(torch.uint8).contiguous()
-    s = sc.contiguous()
-    x = torch.randn(m, k, generator=g).to(torch.bfloat16).to(DEV)
+def test_noalloc_matches_oracle_and_scratch_entry(m, n, k):
+    x, w8, s, oracle = case(m, n, k)
     ref = reference_call(x, w8, s)
     for _ in range(2):
-        rc, out = noalloc_call(x, w8, s)
+        rc, out = noalloc_call(x, w8, s, dtype=torch.float32)
         torch.cuda.synchronize()
         assert rc == 0, N.lib().fp4x_last_error_message().decode()
-        assert rel(out, ref) < 1e-2
+        got = out.cpu().double().numpy()
+        assert np.abs(got - oracle).max() / np.abs(oracle).max() < 5e-5
+        rc, outb = noalloc_call(x, w8, s)
+        torch.cuda.synchronize()
+        assert rc == 0, N.lib().fp4x_last_error_message().decode()
+        assert rel(outb, ref) < 1e-2
     assert N.device_error() == 0
+
+
+def test_noalloc_counters_are_reset_after_a_device_error():
+    """A wait that gives up can leave static counters mid-count; clearing the device error word zeroes them.  The
+    leftover count is planted on the host (a counter write), the error word is set by a bounded wait that expires on
+    purpose (nothing faults), and after the clear the entry point gives the oracle's answer again."""
+    x, w8, s, oracle = case(3, 16384, 2560)  # a stream-K plan: its row blocks use the static counters
+    st = N.stream_of(x)
+    for i in range(4):
+        assert N.lib().fp4x_test_set_static_counter(i, 5, st) == 0
+    assert N.lib().fp4x_test_expire_wait(1000000, st) == 0
+    code = N.device_error(clear=True)
+    assert code == 1
+    assert N.device_error() == 0
+    for _ in range(2):
+        rc, out = noalloc_call(x, w8, s, dtype=torch.float32)
+        torch.cuda.synchronize()
+        assert rc == 0
+        got = out.cpu().double().numpy()
+        assert np.abs(got - oracle).max() / np.abs(oracle).max() < 5e-5
 
 
 def test_noalloc_rejects_shapes_beyond_static_scratch():
