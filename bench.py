@@ -193,7 +193,7 @@ class ClockSampler:
 class DecodeStep:
     """Random-init weights of the step, resident in HBM, and the step itself through the public API."""
 
-    def __init__(self, device, m, layers, rank, world, seed=0):
+    def __init__(self, device, m, layers, rank, world, seed=0, step_kernel=False, serial=True):
         import fp4x_kernels as F
         from fp4x_shard import ShardedFastHead, shard_range
         self.F = F
@@ -237,7 +237,30 @@ class DecodeStep:
         self.streams = torch.randn(m, HCN * HID, device=device, generator=gx).to(torch.bfloat16)
         self.graph = None
         self.result = None
+        self.prog = self.build_program(serial) if step_kernel and m <= 8 else None
         torch.cuda.synchronize(device)
+
+    def build_program(self, serial):
+        """The 48 layers as one persistent launch (F.StepProgram): every op writes its own output buffer; the
+        hyper-connection up output of a layer is the next layer's hidden row."""
+        F, m, dev = self.F, self.m, self.dev
+        prog = F.StepProgram(dev, m, serial=serial)
+        h = self.h0
+        self.step_outs = []
+        for L in self.layers:
+            o = {k: torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+                 for k, n in (("q", QKVZ), ("o", HID), ("t", W6_IN), ("g", GATE), ("di", LR), ("bot", LR),
+                              ("hn", HID))}
+            prog.nv4(h, *L["nv4"], o["q"])
+            prog.w6(o["q"][:, :W6_IN], *L["w6a"], o["o"])
+            prog.w6(o["o"], *L["w6b"], o["t"])
+            prog.w8(h, *L["gate"], o["g"])
+            prog.hc_down(self.streams, L["qd"], L["sd"], o["di"], o["bot"], LR, HCN)
+            prog.hc_up(o["bot"], L["qi"], L["si"], self.streams, o["hn"], HCN, 8)
+            self.step_outs.append(o)
+            h = o["hn"]
+        self.h_last = h
+        return prog.prepare()
 
     # one layer through the drop-in API
     def layer(self, L, h):
@@ -250,9 +273,13 @@ class DecodeStep:
         return self.F.HCFused.up(bot, L["qi"], L["si"], self.streams, HCN, (8, 64, 8))
 
     def body(self):
-        h = self.h0
-        for L in self.layers:
-            h = self.layer(L, h)
+        if self.prog is not None:
+            self.prog.run()
+            h = self.h_last
+        else:
+            h = self.h0
+            for L in self.layers:
+                h = self.layer(L, h)
         if self.world == 1:  # one shard: the head's own argmax is the answer, no merge
             coarse, exact, gidx, _, amax = self.head.local(h, argmax=True)
             return coarse, exact, gidx, amax
@@ -363,6 +390,13 @@ def time_graph_class(step, name, reps=5):
     per_launch_us = e0.elapsed_time(e1) * 1e3 / (reps * len(step.layers))
     del g
     return per_launch_us
+
+
+def time_step_kernel(step, reps=5):
+    """Average device time of the persistent step kernel alone (48 layers in one launch), graph replays."""
+    if step.prog is None:
+        return None
+    return _graph_us(step.prog.run, step.dev, reps)
 
 
 def time_head(step, reps=5):
@@ -720,7 +754,7 @@ def native_arm(args):
     init_dist(world, local, "nccl")
     m = args.m
 
-    step = DecodeStep(dev, m, args.layers, rank, world)
+    step = DecodeStep(dev, m, args.layers, rank, world, step_kernel=args.step_kernel, serial=args.serial)
     launches_per_step = step.capture() + step.merge_launches()
 
     # inputs/results of the end-to-end leg: pinned host buffers
@@ -775,17 +809,22 @@ def native_arm(args):
 
     # dominant kernel class, timed alone
     per_class = {name: time_graph_class(step, name) for name in CLASSES}
+    step_us = time_step_kernel(step)
     exchange = step.exchange_timings()
     exchange = {k: max_over_ranks(v, world, dev) for k, v in exchange.items()}
     head_us = exchange["head_us"]
-    shares = {name: us * args.layers for name, us in per_class.items()}
-    shares["fast_head"] = head_us
-    top = max(shares, key=shares.get)
     peak, peak_kind = peaks()
-    if top == "fast_head":
-        top_bytes, top_us = head_bytes(m, step.v1 - step.v0), head_us
+    if step_us is not None:
+        # one launch runs every layer: it is the dominant kernel of the step
+        top, top_bytes, top_us = "step_kernel", LAYER_BYTES * args.layers, step_us
     else:
-        top_bytes, top_us = CLASSES[top], per_class[top]
+        shares = {name: us * args.layers for name, us in per_class.items()}
+        shares["fast_head"] = head_us
+        top = max(shares, key=shares.get)
+        if top == "fast_head":
+            top_bytes, top_us = head_bytes(m, step.v1 - step.v0), head_us
+        else:
+            top_bytes, top_us = CLASSES[top], per_class[top]
     achieved = top_bytes / (top_us * 1e-6) / 1e9
 
     heads = head_sweep(step) | mixer_sweep(step) if (world == 1 and not args.no_sweep) else None
@@ -805,6 +844,10 @@ def native_arm(args):
                                    f"W6 2560x4096, W6 4096x2560, W8 gate 512x2560, fused HC W8 mixer) + fast LM "
                                    f"head {VOCAB} (INT2 g16, top-512, MXFP8 rescore)",
                        "M": m, "layers": args.layers, "cuda_graph": True,
+                       "layers_in": ("one persistent launch, every op after the op before it (single-stream order)"
+                                     if step.prog is not None and args.serial else
+                                     "one persistent launch, ops ordered by their buffer hazards"
+                                     if step.prog is not None else "one launch per GEMV"),
                        "bytes_per_step": total_bytes,
                        "l2": "no flush: every step streams > 20x L2 of distinct weights",
                        "parallelism": "replicas" if world == 1 else f"layer replicas + vocab-sharded head x{world}"},
@@ -813,6 +856,7 @@ def native_arm(args):
                          "frac": round(achieved / peak, 4), "traffic": traffic_for(top),
                          "per_launch_us": round(top_us, 3), "bytes_per_launch": top_bytes},
             "class_us": {k: round(v, 2) for k, v in per_class.items()} | {"fast_head": round(head_us, 2)},
+            "step_kernel_us": None if step_us is None else round(step_us, 2),
             "sharded_head_us": exchange,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "ms_per_step": round(ms_e2e, 4),
@@ -915,6 +959,10 @@ def main():
     ap.add_argument("--layers", type=int, default=48)
     ap.add_argument("--no-sweep", action="store_true", help="skip the per-GEMV M=1..16 sweep (single GPU only)")
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU oracle baseline")
+    ap.add_argument("--step-kernel", action="store_true",
+                    help="run the 48 layers as one persistent launch (F.StepProgram) instead of one launch per GEMV")
+    ap.add_argument("--dataflow", dest="serial", action="store_false",
+                    help="with --step-kernel: order ops by their buffer hazards only (default: single-stream order)")
     ap.add_argument("--kernel-class", default=None,
                     help="profiling aid: launch only these kernel classes (comma list or 'all') and exit")
     ap.add_argument("--launches", type=int, default=3, help="launches per class with --kernel-class")

@@ -236,6 +236,63 @@ int fp4x_head_merge(const float* coarse, const float* exact, const int32_t* gidx
                     void* stream);
 
 /* ---------------------------------------------------------------------------------------------------------
+ * Decode step in one persistent launch (no reference counterpart: the reference launches one Triton kernel per
+ * linear, and its decode step is a CUDA graph of those launches, x/fp4patch.py:158-272, README.md:77-79).
+ * An ordered list of the GEMV-family ops of a step runs as one kernel with one CTA per SM: each op computes exactly
+ * what its standalone entry point computes (same weights, rounding and fixed summation order), ops wait only for
+ * the earlier ops whose buffers they read or overwrite, and the weight stream of later ops is loaded while earlier
+ * ops finish.  M <= 8 tokens.
+ * --------------------------------------------------------------------------------------------------------- */
+#define FP4X_STEP_NV4 0      /* nv4_linear: x [M, k] -> out [M, n], gs global scale */
+#define FP4X_STEP_W6 1       /* w6_linear: p0 = low nibbles, p1 = high bit pairs, s = fp16 scales */
+#define FP4X_STEP_W8 2       /* w8_linear: p0 = int8 codes, s = fp32 scales */
+#define FP4X_STEP_HC_DOWN 3  /* fp4x_hc_down: out = di [M, n], out2 = bot [M, lr] */
+#define FP4X_STEP_HC_UP 4    /* fp4x_hc_up: x = bot, p0/s = interleaved up rows, nrm, out [M, n / hc] */
+#define FP4X_STEP_MX8 5      /* mx8_linear: p0 = e4m3 codes, s = e8m0 scales */
+
+typedef struct fp4x_step_op {
+  int kind;                /* FP4X_STEP_* */
+  const void* x;           /* bf16 [M, k] activations, row stride x_stride elements */
+  int64_t x_stride;
+  const void* p0;          /* weight plane 0 */
+  const void* p1;          /* weight plane 1 (W6 high bit pairs), else NULL */
+  const void* s;           /* scales */
+  float gs;                /* NVFP4 global scale */
+  void* out;               /* [M, n] (row stride out_stride elements, out_dtype) */
+  void* out2;              /* HC down: bot */
+  int64_t out_stride;
+  int out_dtype;
+  int64_t n, k;
+  int64_t lr, hc, bj;      /* hyper-connection ops */
+  const void* nrm;         /* HC up: normalized streams [M, n] */
+  int64_t nrm_stride;
+} fp4x_step_op;
+
+/* Sizes for a step of `count` ops at m tokens: device op table (64-byte aligned), workspace, int32 counters.
+ * serial != 0 makes every op also wait for the op before it (the order of a single stream); otherwise ops wait
+ * only for the earlier ops whose buffers they read or overwrite. */
+int fp4x_step_query(const fp4x_step_op* ops, int64_t count, int64_t m, int serial, size_t* table_bytes,
+                    size_t* ws_bytes, int64_t* n_counters);
+
+/* Plans the ops, orders them by their buffer hazards and writes the device op table (one synchronous copy; run it
+ * outside stream capture).  The workspace and the zeroed counters belong to the step until fp4x_step_release; the
+ * counters are left zero after every completed run.  Buffers named by the ops must stay allocated. */
+int fp4x_step_prepare(const fp4x_step_op* ops, int64_t count, int64_t m, int serial, void* table, size_t table_bytes,
+                      void* ws, size_t ws_bytes, int32_t* counters, int64_t n_counters);
+
+/* Runs a prepared step on `stream` (one launch; capturable in a CUDA graph).  Runs of one step must not overlap. */
+int fp4x_step_run(const void* table, void* stream);
+
+/* Diagnostic (no reference counterpart): with trace non-NULL, later runs of the step write a timeline to it:
+ * [CTAs][ops][8] globaltimer nanoseconds at which each CTA started the op, had its inputs, had staged them,
+ * finished it, had its first weight stage, left its stage loop and finished its last split-K flush (0 where a CTA
+ * has no work in the op; the last entry is unused).  trace = NULL turns it off. */
+int fp4x_step_trace(const void* table, uint64_t* trace, int64_t entries);
+
+/* Forgets a prepared step (host bookkeeping only). */
+int fp4x_step_release(const void* table);
+
+/* ---------------------------------------------------------------------------------------------------------
  * Weight preparation on the GPU (replaces the reference's torch quantizers and dequantizers, K:138-357, and the
  * lazy preparation of x/fp4patch.py:61-83, :206-214, :290-307).  Inputs are row-major [n, k] weights in fp32, bf16
  * or f16 (FP4X_IN_*); outputs are the packed layouts listed at the top of this file.

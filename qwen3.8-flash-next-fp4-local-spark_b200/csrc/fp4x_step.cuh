@@ -20,9 +20,11 @@ namespace fp4x {
 
 constexpr int kStepMaxDeps = 6;
 constexpr int kStepMaxStages = 12;
+constexpr int kStepSlotBytes = 18432;  // stage pitch: the largest stage of the step formats (NVFP4, 64 x 288 bytes)
 
 // One op of a step: the standalone GEMV's argument block (geometry, TMA descriptors, pointers, plan) plus the
-// dispatch keys and dependencies.  In a step, a.STG is the ring's stage pitch and a.CPP the number of CTAs.
+// dispatch keys and dependencies.  In a step, a.STG is the ring's stage pitch and a.CPP the number of CTAs that
+// share the op's units.
 struct alignas(64) StepOp {
   GemvArgs a;
   int fmt, epi, shape;
@@ -34,12 +36,19 @@ struct StepArgs {
   const StepOp* ops;
   int nops;
   int NS;              // ring stages
-  int SLOT;            // stage pitch (bytes, multiple of 1024)
-  int smem_x, smem_misc, smem_scr, smem_comb;
+  int SLOT;            // stage pitch (bytes, multiple of 1024): kStepSlotBytes
+  int smem_x, smem_xraw, smem_misc, smem_scr, smem_comb;
   int* done;           // [nops] CTAs that finished each op; zero on entry, zeroed again by the last CTA to finish
   int* fin;            // CTAs that finished the whole step
   int* err;            // device error word
+  uint64_t* trace;     // optional timeline: [grid][nops][8] globaltimer stamps written by consumer thread 0: op
+                       // start, inputs ready, staged, done, first weight stage ready, stage loop done, last flush
+                       // done; null when off
 };
+
+FP4X_DEV void step_stamp(const StepArgs& S, int j, int what) {
+  if (S.trace && threadIdx.x == 0) S.trace[((int64_t)blockIdx.x * S.nops + j) * 8 + what] = global_ns();
+}
 
 FP4X_DEV int ld_acquire_gpu(const int* p) {
   int v;
@@ -64,15 +73,19 @@ FP4X_DEV bool step_wait(uint32_t bar, uint32_t parity, int* err) {
   }
 }
 
-// the unit range [u_begin, u_end) of CTA `cta` of G in an op (whole plans: whole row blocks)
-FP4X_DEV void step_units(const GemvArgs& A, int G, int cta, int64_t& ub, int64_t& ue) {
-  if (A.whole) {
-    ub = range_begin(A.RT, G, cta) * A.NCH;
-    ue = range_begin(A.RT, G, cta + 1) * A.NCH;
+// the unit range [u_begin, u_end) of CTA `cta` in an op: the op's units are split over its first A.CPP CTAs
+// (min(CTAs, units): every one of them owns at least one unit); whole plans take whole row blocks
+FP4X_DEV void step_units(const GemvArgs& A, int cta, int64_t& ub, int64_t& ue) {
+  const int W = A.CPP;
+  if (cta >= W) {
+    ub = ue = 0;
+  } else if (A.whole) {
+    ub = range_begin(A.RT, W, cta) * A.NCH;
+    ue = range_begin(A.RT, W, cta + 1) * A.NCH;
   } else {
     const int64_t Up = (int64_t)A.RT * A.NCH;
-    ub = range_begin(Up, G, cta);
-    ue = range_begin(Up, G, cta + 1);
+    ub = range_begin(Up, W, cta);
+    ue = range_begin(Up, W, cta + 1);
   }
 }
 
@@ -80,8 +93,8 @@ FP4X_DEV void step_units(const GemvArgs& A, int G, int cta, int64_t& ub, int64_t
 // producer: the weight tiles of one op's units into the ring (the standalone producer loop, ring state carried over)
 // ---------------------------------------------------------------------------------------------------------------
 template <int FMT>
-FP4X_DEV bool step_produce(const GemvArgs& A, int64_t ub, int64_t ue, uint8_t* base, int SLOT, int NS, uint32_t full0,
-                           uint32_t empty0, int& s, int& round, int* err) {
+__device__ __noinline__ bool step_produce(const GemvArgs& A, int64_t ub, int64_t ue, uint8_t* base, int SLOT, int NS, uint32_t full0,
+                           uint32_t empty0, int& s, int& round, int& issued, int* err) {
   constexpr FmtGeom G = fmt_geom(FMT);
   const int lane = threadIdx.x & 31;
   const int tx = kRB * (A.NB0 * A.BI0 + (G.n1 ? A.BI1 : 0));
@@ -114,6 +127,7 @@ FP4X_DEV bool step_produce(const GemvArgs& A, int64_t ub, int64_t ue, uint8_t* b
       }
     }
     cp_async_arrive_noinc(bar);
+    ++issued;
     if (++s == NS) { s = 0; ++round; }
     if (++chunk == A.NCH) { chunk = 0; ++blk; }
   }
@@ -121,41 +135,44 @@ FP4X_DEV bool step_produce(const GemvArgs& A, int64_t ub, int64_t ue, uint8_t* b
 }
 
 // ---------------------------------------------------------------------------------------------------------------
-// activation staging of a k range: chunks c_lo .. c_lo + nc - 1 (mod NCH) of the op's K, read from L2 (another SM
-// wrote them), laid out as a local panel of nc chunks in the format's permuted B order
+// activation staging of a k range: chunks c_lo .. c_lo + nc - 1 (mod NCH) of the op's K.  Every consumer thread
+// issues its 16-byte asynchronous copies of the raw bf16 rows at once (L2 only: other SMs wrote them), so the
+// staging costs one L2 round trip; then the rows are converted from shared memory into a local panel of nc chunks
+// in the format's permuted B order.
 // ---------------------------------------------------------------------------------------------------------------
 template <int FMT>
-FP4X_DEV void step_stage(const GemvArgs& A, uint8_t* base, int smem_x, int smem_misc, int XP, int c_lo, int nc) {
+FP4X_DEV void step_stage(const GemvArgs& A, uint8_t* base, int smem_x, int smem_xraw, int smem_misc, int XP, int c_lo,
+                         int nc) {
   constexpr FmtGeom G = fmt_geom(FMT);
   constexpr int nthr = kCWarps * 32;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(A.item.x);
   const int64_t xs = A.x_stride;
-  const int bpc = A.KC / G.qb;     // staging blocks per chunk
-  const int nblk = nc * bpc;
-  float* xsc = reinterpret_cast<float*>(base + smem_misc);  // [8] scale, [8] inverse (per token)
-  auto kstart = [&](int lb) -> int {  // global k of local staging block lb
-    const int lc = lb / bpc;
+  const int kloc = nc * A.KC;   // local k extent
+  const int vpr = kloc / 8;     // 16-byte vectors per token row
+  const uint32_t raw = smem_u32(base + smem_xraw);
+  for (int i = tid; i < A.M * vpr; i += nthr) {
+    const int tok = i / vpr, lk = (i - tok * vpr) * 8;
+    const int lc = lk / A.KC;
     int c = c_lo + lc;
     if (c >= A.NCH) c -= A.NCH;
-    return c * A.KC + (lb - lc * bpc) * G.qb;
-  };
+    cp_async16(raw + (uint32_t)(tok * kloc + lk) * 2u, x + (int64_t)tok * xs + c * A.KC + (lk - lc * A.KC));
+  }
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  named_bar(1, nthr);
+  const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(base + smem_xraw);
+  float* xsc = reinterpret_cast<float*>(base + smem_misc);  // [8] scale, [8] inverse (per token)
   if (G.xf16) {
     for (int tok = warp; tok < A.M; tok += kCWarps) {
       float mx = 0.f;
-      const __nv_bfloat16* row = x + (int64_t)tok * xs;
-      for (int lc = 0; lc < nc; ++lc) {
-        int c = c_lo + lc;
-        if (c >= A.NCH) c -= A.NCH;
-        const uint4* p = reinterpret_cast<const uint4*>(row + (int64_t)c * A.KC);
-        for (int i = lane; i < A.KC / 8; i += 32) {
-          const uint4 v = __ldcg(p + i);
-          const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+      const uint4* row = reinterpret_cast<const uint4*>(xr + (int64_t)tok * kloc);
+      for (int i = lane; i < vpr; i += 32) {
+        const uint4 v = row[i];
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            mx = fmaxf(mx, fabsf(bf16_bits_to_f32(w[e] & 0xffffu)));
-            mx = fmaxf(mx, fabsf(bf16_bits_to_f32(w[e] >> 16)));
-          }
+        for (int e = 0; e < 4; ++e) {
+          mx = fmaxf(mx, fabsf(bf16_bits_to_f32(w[e] & 0xffffu)));
+          mx = fmaxf(mx, fabsf(bf16_bits_to_f32(w[e] >> 16)));
         }
       }
 #pragma unroll
@@ -174,31 +191,98 @@ FP4X_DEV void step_stage(const GemvArgs& A, uint8_t* base, int smem_x, int smem_
     named_bar(1, nthr);
   }
   const uint32_t xbase = smem_u32(base + smem_x);
-  for (int tok = 0; tok < A.M; ++tok)
-    for (int lb = tid; lb < nblk; lb += nthr) {
-      const float scl = G.xf16 ? xsc[tok] : 1.f;
-      uint32_t v[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-      const __nv_bfloat16* src = x + (int64_t)tok * xs + kstart(lb);
-      if (G.qb == 4) {
-        const uint2 t = __ldcg(reinterpret_cast<const uint2*>(src));
-        v[0] = t.x; v[1] = t.y;
-      } else {
-        const uint4 t = __ldcg(reinterpret_cast<const uint4*>(src));
-        v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
-      }
-      int sp[4];
-      int tq;
-      stage_block_positions<FMT>(lb, sp, tq);
-      const uint32_t trow = xbase + tok * XP;
-      if (G.qb == 4) {
-        sts64(trow + sp[0] * 32 + tq * 8, cvt_pair(v[0], scl, G.xf16), cvt_pair(v[1], scl, G.xf16));
-      } else {  // W6: elements r0..r7; quads (r0,r4,r1,r5) and (r2,r6,r3,r7)
-        sts64(trow + sp[0] * 32 + tq * 8, cvt_pair(pick2(v[0], 0, v[2], 0), scl, G.xf16),
-              cvt_pair(pick2(v[0], 1, v[2], 1), scl, G.xf16));
-        sts64(trow + sp[1] * 32 + tq * 8, cvt_pair(pick2(v[1], 0, v[3], 0), scl, G.xf16),
-              cvt_pair(pick2(v[1], 1, v[3], 1), scl, G.xf16));
-      }
+  const int nblk = kloc / G.qb;
+  for (int i = tid; i < A.M * nblk; i += nthr) {
+    const int tok = i / nblk, lb = i - tok * nblk;
+    const float scl = G.xf16 ? xsc[tok] : 1.f;
+    uint32_t v[4] = {0, 0, 0, 0};
+    const uint32_t src = raw + (uint32_t)(tok * kloc + lb * G.qb) * 2u;
+    if (G.qb == 4) {
+      const uint2 t = lds64(src);
+      v[0] = t.x; v[1] = t.y;
+    } else {
+      const uint4 t = lds128(src);
+      v[0] = t.x; v[1] = t.y; v[2] = t.z; v[3] = t.w;
     }
+    int sp[4];
+    int tq;
+    stage_block_positions<FMT>(lb, sp, tq);
+    const uint32_t trow = xbase + tok * XP;
+    if (G.qb == 4) {
+      sts64(trow + sp[0] * 32 + tq * 8, cvt_pair(v[0], scl, G.xf16), cvt_pair(v[1], scl, G.xf16));
+    } else {  // W6: elements r0..r7; quads (r0,r4,r1,r5) and (r2,r6,r3,r7)
+      sts64(trow + sp[0] * 32 + tq * 8, cvt_pair(pick2(v[0], 0, v[2], 0), scl, G.xf16),
+            cvt_pair(pick2(v[0], 1, v[2], 1), scl, G.xf16));
+      sts64(trow + sp[1] * 32 + tq * 8, cvt_pair(pick2(v[1], 0, v[3], 0), scl, G.xf16),
+            cvt_pair(pick2(v[1], 1, v[3], 1), scl, G.xf16));
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------------------------------------------
+// epilogues: the standalone ones, except that the hyper-connection up epilogue synchronises its warp pair (32
+// interleaved rows = 8 output columns x 4 streams) through an mbarrier with a bounded wait instead of a named
+// barrier, so a warp that stopped on an error cannot leave its partner waiting for ever
+// ---------------------------------------------------------------------------------------------------------------
+FP4X_DEV bool pair_sync(uint32_t bar, uint32_t& count, int* err) {
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+  const bool ok = step_wait(bar, count & 1u, err);
+  ++count;
+  __syncwarp();
+  return ok;
+}
+
+template <int EPI, int NT>
+FP4X_DEV bool step_epilogue(const GemvArgs& A, int row0, const float (&v)[NT][4], int warp, int g, int tq,
+                            float* scr_all, uint32_t pair0, uint32_t& npair, int* err) {
+  if (EPI != EPI_HC_UP) {
+    run_epilogue<EPI, NT>(A, A.item, row0, v, warp, g, tq, scr_all);
+    return true;
+  }
+  constexpr int MP = 8 * NT;
+  float* scr = scr_all + warp * 16 * MP;
+#pragma unroll
+  for (int t = 0; t < NT; ++t)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const int r = g + 8 * (e >> 1);
+      const int m = 8 * t + 2 * tq + (e & 1);
+      scr[r * MP + m] = bf16_round(sigmoidf_(bf16_round(v[t][e])));
+    }
+  const int rows = A.hc * A.bj;
+  const int lane = 4 * g + tq;
+  int first_warp = warp, nwarps = 1;
+  const uint32_t bar = pair0 + 8 * (warp >> 1);
+  if (rows == 32) {
+    first_warp = warp & ~1;
+    nwarps = 2;
+    if (!pair_sync(bar, npair, err)) return false;
+  } else {
+    __syncwarp();
+  }
+  const float* bscr = scr_all + first_warp * 16 * MP;
+  const int blk_row0 = row0 - 16 * (warp - first_warp);
+  if (blk_row0 < A.N) {
+    const int jb = blk_row0 / rows;
+    const int H = A.N / A.hc;
+    const __nv_bfloat16* nrm = reinterpret_cast<const __nv_bfloat16*>(A.nrm);
+    const int nout = A.bj * A.M;
+    for (int o = lane + 32 * (warp - first_warp); o < nout; o += 32 * nwarps) {
+      const int m = o / A.bj, cidx = o - m * A.bj;
+      const int col = jb * A.bj + cidx;
+      float nv[8], gv[8];
+      for (int s = 0; s < A.hc; ++s) {
+        nv[s] = __bfloat162float(nrm[(int64_t)m * A.nrm_stride + s * H + col]);
+        gv[s] = bscr[(s * A.bj + cidx) * MP + m];
+      }
+      reinterpret_cast<__nv_bfloat16*>(A.item.out)[(int64_t)m * A.out_stride + col] =
+          __float2bfloat16_rn(hc_gate_mean(nv, gv, A.hc));
+    }
+  }
+  if (rows == 32) return pair_sync(bar, npair, err);
+  __syncwarp();
+  return true;
 }
 
 // ---------------------------------------------------------------------------------------------------------------
@@ -208,31 +292,137 @@ struct StepConsumerState {
   int s;
   uint32_t phase;
   uint32_t nflush;
+  uint32_t npair;  // hyper-connection up: warp-pair handshakes so far (mbarrier parity)
+  int consumed;    // stages this warp has taken from the ring
 };
 
-template <int FMT, int NT, int EPI, int SHAPE>
-FP4X_DEV bool step_consume(const StepArgs& S, const StepOp& op, int64_t ub, int64_t ue, uint8_t* base,
-                           uint32_t full0, uint32_t empty0, uint32_t comb_full0, uint32_t comb_empty0,
-                           StepConsumerState& st) {
+// stage geometry of each format in a step (compile-time, so the hot loop keeps no geometry in registers)
+template <int FMT>
+struct StepGeom {
+  static constexpr int KC = FMT == FMT_NV4 ? 512 : 256;            // k per stage
+  static constexpr int NB0 = FMT == FMT_W6 ? 1 : 2;                // 128-byte plane-0 boxes per stage
+  static constexpr int BI1 = FMT == FMT_W6 ? 64 : 0;               // plane-1 box bytes
+  static constexpr int SB = FMT == FMT_NV4 ? 32 : (FMT == FMT_MX8 ? 8 : 16);  // scale bytes per row
+  static constexpr int SHAPE = FMT == FMT_W6 ? SHAPE_128x1 : SHAPE_128x2;
+  static constexpr int OFF_P1 = kRB * NB0 * 128;
+  static constexpr int OFF_SC = OFF_P1 + kRB * BI1;
+};
+
+// Split-K flush of one row block (k-group hand-over, partial slot, last-arriver sum, epilogue); out of line so
+// that the stage loop keeps none of its state in registers.
+template <int FMT, int EPI>
+__device__ __noinline__ bool step_flush(const StepArgs& S, const StepOp& op, int blk, float (&acc)[1][4],
+                                        uint8_t* base, uint32_t comb_full0, uint32_t comb_empty0,
+                                        StepConsumerState& st) {
   constexpr FmtGeom G = fmt_geom(FMT);
-  constexpr int MP = 8 * NT;
+  constexpr int NT = 1, MP = 8;
   const GemvArgs& A = op.a;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, tq = lane & 3;
   const int wrow = warp & (kRW - 1), kg = warp / kRW;
   const int cta = blockIdx.x, CPP = A.CPP;
-  const int64_t nunits = ue - ub;
+  float* comb = reinterpret_cast<float*>(base + S.smem_comb) + (wrow * 32 + lane) * (NT * 4);
+  const uint32_t pair0 = comb_empty0 + 8 * kRW;  // two warp-pair barriers after the k-group handshakes
+  float* scr = reinterpret_cast<float*>(base + S.smem_scr);
+  const uint32_t cf_bar = comb_full0 + 8 * wrow, ce_bar = comb_empty0 + 8 * wrow;
+  const uint32_t par = st.nflush & 1u;
+  ++st.nflush;
+  if (kg == 1) {
+    if (st.nflush > 1 && !step_wait(ce_bar, par ^ 1u, S.err)) return false;
+    *reinterpret_cast<float4*>(comb) = make_float4(acc[0][0], acc[0][1], acc[0][2], acc[0][3]);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(cf_bar);
+    return true;
+  }
+  if (!step_wait(cf_bar, par, S.err)) return false;
+  {
+    const float4 o = *reinterpret_cast<const float4*>(comb);
+    acc[0][0] += o.x; acc[0][1] += o.y; acc[0][2] += o.z; acc[0][3] += o.w;
+  }
+  __syncwarp();
+  if (lane == 0) mbar_arrive(ce_bar);
+  if (G.xf16) {
+    const float* xsc = reinterpret_cast<const float*>(base + S.smem_misc);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[0][e] *= xsc[8 + 2 * tq + (e & 1)];
+  }
+  const int row0 = blk * kRB + 16 * wrow;
+  const int Up = A.whole ? A.RT : A.RT * A.NCH;
+  int cf, cl;
+  if (A.whole) {
+    cf = cl = cta;
+  } else {
+    const int uf = blk * A.NCH, ul = uf + A.NCH - 1;
+    cf = owner_of(uf, Up, CPP);
+    cl = owner_of(ul, Up, CPP);
+  }
+  const int segs = cl - cf + 1;
+  if (segs == 1) return step_epilogue<EPI, NT>(A, row0, acc, wrow, g, tq, scr, pair0, st.npair, S.err);
+  auto slot_of = [&](int cc) -> int64_t {  // a CTA shares at most two blocks: its first (slot 0) and last (1)
+    const int first_blk = (int)(range_begin(Up, CPP, cc) / A.NCH);
+    return ((int64_t)cc * 2 + (blk == first_blk ? 0 : 1)) * kRW + wrow;
+  };
+  float* mine = A.ws + slot_of(cta) * (16 * MP);
+  __stcg(reinterpret_cast<float2*>(mine + g * MP + 2 * tq), make_float2(acc[0][0], acc[0][1]));
+  __stcg(reinterpret_cast<float2*>(mine + (g + 8) * MP + 2 * tq), make_float2(acc[0][2], acc[0][3]));
+  __syncwarp();
+  int* semp = A.sem + blk * kRW + wrow;
+  int last = 0;
+  if (lane == 0) last = (atomic_add_acq_rel(semp, 1) == segs - 1);
+  last = __shfl_sync(0xffffffffu, last, 0);
+  __syncwarp();
+  if (!last) return true;
+  float tot[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+  constexpr int kBatch = 16;  // every slot load of a batch is in flight before the first is added
+  for (int i0 = 0; i0 < segs; i0 += kBatch) {
+    float2 v[kBatch][2];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      if (i0 + j < segs) {
+        const float* src = A.ws + slot_of(cf + i0 + j) * (16 * MP);
+        v[j][0] = __ldcg(reinterpret_cast<const float2*>(src + g * MP + 2 * tq));
+        v[j][1] = __ldcg(reinterpret_cast<const float2*>(src + (g + 8) * MP + 2 * tq));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      if (i0 + j < segs) {
+        tot[0][0] += v[j][0].x; tot[0][1] += v[j][0].y;
+        tot[0][2] += v[j][1].x; tot[0][3] += v[j][1].y;
+      }
+    }
+  }
+  const bool ok = step_epilogue<EPI, NT>(A, row0, tot, wrow, g, tq, scr, pair0, st.npair, S.err);
+  if (lane == 0) atomicExch(semp, 0);
+  return ok;
+}
+
+// One op's units of this CTA: wait for the op's dependencies, stage the activations, consume the weight stages and
+// flush each row block.  The ring position and the flush / pair counters carry over from op to op in `st`.
+template <int FMT, int EPI>
+__device__ __noinline__ bool step_consume(const StepArgs& S, const StepOp& op, int ub, int ue, uint8_t* base,
+                                          uint32_t full0, uint32_t empty0, uint32_t comb_full0,
+                                          uint32_t comb_empty0, StepConsumerState& st) {
+  using SG = StepGeom<FMT>;
+  constexpr int NT = 1;
+  const GemvArgs& A = op.a;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, tq = lane & 3;
+  const int wrow = warp & (kRW - 1), kg = warp / kRW;
+  const int grid = gridDim.x;
+  const int nunits = ue - ub;
+  const int NCH = A.NCH;
   int* abort_flag = reinterpret_cast<int*>(base + S.smem_misc + 64);
 
   // 1. dependencies: thread 0 waits until every op this one depends on has been finished by all CTAs
   if (threadIdx.x == 0) {
     int bad = 0;
     for (int d = 0; d < op.ndeps && !bad; ++d) {
-      const int* cnt = S.done + op.deps[d];
-      if (ld_acquire_gpu(cnt) >= CPP) continue;
+      const int* cnt = S.done + op.deps[d];  // every CTA of the grid counts itself in when it is done with an op
+      if (ld_acquire_gpu(cnt) >= grid) continue;
       const uint64_t t0 = global_ns();
       for (uint32_t it = 1;; ++it) {
-        if (ld_acquire_gpu(cnt) >= CPP) break;
+        if (ld_acquire_gpu(cnt) >= grid) break;
         if ((it & 63u) == 0) {
           if (ld_volatile(S.err)) { bad = 1; break; }
           if (global_ns() - t0 > 2000000000ull) {
@@ -247,156 +437,74 @@ FP4X_DEV bool step_consume(const StepArgs& S, const StepOp& op, int64_t ub, int6
   }
   named_bar(1, kCWarps * 32);
   if (*reinterpret_cast<volatile int*>(abort_flag)) return false;
+  step_stamp(S, (int)(&op - S.ops), 1);
 
   // 2. activations of the CTA's k range
-  int c_lo = 0, nc = A.NCH;
-  if (!A.whole && nunits < A.NCH) {
-    c_lo = (int)(ub % A.NCH);
-    nc = (int)nunits;
+  int c_lo = 0, nc = NCH;
+  if (!A.whole && nunits < NCH) {
+    c_lo = ub % NCH;
+    nc = nunits;
   }
-  const int steps_per_stage = A.KC / 16;
-  const int XP = nc * steps_per_stage * 32 + 32;
-  step_stage<FMT>(A, base, S.smem_x, S.smem_misc, XP, c_lo, nc);
+  constexpr int kSteps = SG::KC / 16;  // mma k-steps per stage
+  const int XP = nc * kSteps * 32 + 32;
+  step_stage<FMT>(A, base, S.smem_x, S.smem_xraw, S.smem_misc, XP, c_lo, nc);
   named_bar(1, kCWarps * 32);
+  step_stamp(S, (int)(&op - S.ops), 2);
 
-  const float* xsc = reinterpret_cast<const float*>(base + S.smem_misc);
-  float* scr = reinterpret_cast<float*>(base + S.smem_scr);
+  // 3. the stage loop: geometry is compile-time; the loop keeps the ring position, the chunk and the warp context
   WarpCtx wc;
-  wc.BI0 = A.BI0; wc.BI1 = A.BI1; wc.NB0 = A.NB0; wc.SB = A.SB; wc.XP = XP; wc.CPB = A.BI0 / 16;
+  wc.BI0 = 128; wc.BI1 = SG::BI1; wc.NB0 = SG::NB0; wc.SB = SG::SB; wc.XP = XP; wc.CPB = 8;
   wc.g = g; wc.tq = tq; wc.rbase = 16 * wrow;
   wc.gshift = 0;
   {
     const int r = 16 * wrow + (lane & 7) + 8 * ((lane >> 3) & 1);
-    wc.lrow0 = (uint32_t)(r * A.BI0);
-    wc.lswz = A.BI0 == 128 ? (r & 7) : ((r >> 1) & 3);
+    wc.lrow0 = (uint32_t)(r * 128);
+    wc.lswz = r & 7;
     wc.lsel = lane >> 4;
   }
   // B rows at or beyond M read token M-1 (only M rows are staged; those columns are never stored)
   const int grow = g < A.M ? g : A.M - 1;
   const uint32_t xrow = smem_u32(base + S.smem_x) + grow * XP + tq * 8;
-  const int64_t Up = A.whole ? (int64_t)A.RT : (int64_t)A.RT * A.NCH;
-  float* comb = reinterpret_cast<float*>(base + S.smem_comb) + (wrow * 32 + lane) * (NT * 4);
-  bool ok = true;
-
-  auto flush = [&](int blk, float (&acc)[NT][4]) {
-    const uint32_t cf_bar = comb_full0 + 8 * wrow, ce_bar = comb_empty0 + 8 * wrow;
-    const uint32_t par = st.nflush & 1u;
-    ++st.nflush;
-    if (kg == 1) {
-      if (st.nflush > 1 && !step_wait(ce_bar, par ^ 1u, S.err)) { ok = false; return; }
-#pragma unroll
-      for (int t = 0; t < NT; ++t)
-        *reinterpret_cast<float4*>(comb + 4 * t) = make_float4(acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
-      __syncwarp();
-      if (lane == 0) mbar_arrive(cf_bar);
-      return;
-    }
-    if (!step_wait(cf_bar, par, S.err)) { ok = false; return; }
-#pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      const float4 o = *reinterpret_cast<const float4*>(comb + 4 * t);
-      acc[t][0] += o.x; acc[t][1] += o.y; acc[t][2] += o.z; acc[t][3] += o.w;
-    }
-    __syncwarp();
-    if (lane == 0) mbar_arrive(ce_bar);
-    if (G.xf16) {
-#pragma unroll
-      for (int t = 0; t < NT; ++t)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) acc[t][e] *= xsc[8 + min(8 * t + 2 * tq + (e & 1), 7)];
-    }
-    const int row0 = blk * kRB + 16 * wrow;
-    int cf, cl;
-    if (A.whole) {
-      cf = cl = cta;
-    } else {
-      const int64_t uf = (int64_t)blk * A.NCH, ul = uf + A.NCH - 1;
-      cf = owner_of(uf, Up, CPP);
-      cl = owner_of(ul, Up, CPP);
-    }
-    const int segs = cl - cf + 1;
-    if (segs == 1) {
-      run_epilogue<EPI, NT>(A, A.item, row0, acc, wrow, g, tq, scr);
-      return;
-    }
-    auto slot_of = [&](int cc) -> int64_t {  // a CTA shares at most two blocks: its first (slot 0) and last (1)
-      const int first_blk = (int)(range_begin(Up, CPP, cc) / A.NCH);
-      return ((int64_t)cc * 2 + (blk == first_blk ? 0 : 1)) * kRW + wrow;
-    };
-    float* mine = A.ws + slot_of(cta) * (16 * MP);
-#pragma unroll
-    for (int t = 0; t < NT; ++t) {
-      const int m = 8 * t + 2 * tq;
-      __stcg(reinterpret_cast<float2*>(mine + g * MP + m), make_float2(acc[t][0], acc[t][1]));
-      __stcg(reinterpret_cast<float2*>(mine + (g + 8) * MP + m), make_float2(acc[t][2], acc[t][3]));
-    }
-    __syncwarp();
-    int* semp = A.sem + (int64_t)blk * kRW + wrow;
-    int last = 0;
-    if (lane == 0) last = (atomic_add_acq_rel(semp, 1) == segs - 1);
-    last = __shfl_sync(0xffffffffu, last, 0);
-    __syncwarp();
-    if (!last) return;
-    float tot[NT][4];
-    zero4<NT>(tot);
-    constexpr int kBatch = 8 / NT;
-    for (int i0 = 0; i0 < segs; i0 += kBatch) {
-      float2 v[kBatch][NT][2];
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        if (i0 + j < segs) {
-          const float* src = A.ws + slot_of(cf + i0 + j) * (16 * MP);
-#pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            const int m = 8 * t + 2 * tq;
-            v[j][t][0] = __ldcg(reinterpret_cast<const float2*>(src + g * MP + m));
-            v[j][t][1] = __ldcg(reinterpret_cast<const float2*>(src + (g + 8) * MP + m));
-          }
-        }
-      }
-#pragma unroll
-      for (int j = 0; j < kBatch; ++j) {
-        if (i0 + j < segs) {
-#pragma unroll
-          for (int t = 0; t < NT; ++t) {
-            tot[t][0] += v[j][t][0].x; tot[t][1] += v[j][t][0].y;
-            tot[t][2] += v[j][t][1].x; tot[t][3] += v[j][t][1].y;
-          }
-        }
-      }
-    }
-    run_epilogue<EPI, NT>(A, A.item, row0, tot, wrow, g, tq, scr);
-    if (lane == 0) atomicExch(semp, 0);
-  };
-
+  const uint32_t ring = smem_u32(base);
+  const int NS = S.NS;
+  int* err = S.err;
+  int s = st.s;
+  uint32_t phase = st.phase;
   float acc[NT][4];
   zero4<NT>(acc);
-  int cur = -1;
-  int blk = (int)(ub / A.NCH), chunk = (int)(ub - (int64_t)blk * A.NCH);
-  for (int64_t q = ub; q < ue; ++q) {
+  int blk = ub / NCH, chunk = ub - blk * NCH;
+  int cur = blk;
+  bool ok = true;
+  for (int q = ub; q < ue; ++q) {
     if (blk != cur) {
-      if (cur >= 0) {
-        flush(cur, acc);
-        if (!ok) return false;
-      }
+      st.s = s;
+      st.phase = phase;
+      ok = step_flush<FMT, EPI>(S, op, cur, acc, base, comb_full0, comb_empty0, st);
+      if (!ok) break;
       zero4<NT>(acc);
       cur = blk;
     }
-    if (!step_wait(full0 + 8 * st.s, st.phase, S.err)) return false;
-    const uint32_t stage = smem_u32(base) + (uint32_t)st.s * S.SLOT;
+    if (!step_wait(full0 + 8 * s, phase, err)) { ok = false; break; }
+    if (q == ub) step_stamp(S, (int)(&op - S.ops), 4);
+    const uint32_t stage = ring + (uint32_t)s * kStepSlotBytes;
     wc.p0 = stage;
-    wc.p1 = stage + A.off_p1;
-    wc.sc = stage + A.off_sc;
+    wc.p1 = stage + SG::OFF_P1;
+    wc.sc = stage + SG::OFF_SC;
     int lc = chunk - c_lo;
-    if (lc < 0) lc += A.NCH;
-    wc.xb = xrow + lc * steps_per_stage * 32;
-    compute_stage<FMT, NT, SHAPE>(wc, kg, acc);
+    if (lc < 0) lc += NCH;
+    wc.xb = xrow + lc * kSteps * 32;
+    compute_stage<FMT, NT, SG::SHAPE>(wc, kg, acc);
     __syncwarp();
-    if (lane == 0) mbar_arrive(empty0 + 8 * st.s);
-    if (++st.s == S.NS) { st.s = 0; st.phase ^= 1u; }
-    if (++chunk == A.NCH) { chunk = 0; ++blk; }
+    if (lane == 0) mbar_arrive(empty0 + 8 * s);
+    ++st.consumed;
+    if (++s == NS) { s = 0; phase ^= 1u; }
+    if (++chunk == NCH) { chunk = 0; ++blk; }
   }
-  if (cur >= 0) flush(cur, acc);
+  st.s = s;
+  st.phase = phase;
+  step_stamp(S, (int)(&op - S.ops), 5);
+  if (ok) ok = step_flush<FMT, EPI>(S, op, cur, acc, base, comb_full0, comb_empty0, st);
+  step_stamp(S, (int)(&op - S.ops), 6);
   return ok;
 }
 
@@ -411,6 +519,8 @@ enum StepKind : int {
   STEP_KINDS = 6
 };
 
+// 288 threads in one CTA per SM: the 9 warps spread over the 4 SM sub-partitions put 3 warps on one of them, whose
+// 16K-register share then bounds a thread at 168 registers (__launch_bounds__ derives that).
 template <int NT>
 __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant__ StepArgs S) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
@@ -428,6 +538,8 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
       mbar_init(comb_full0 + 8 * i, 1);
       mbar_init(comb_empty0 + 8 * i, 1);
     }
+    for (int i = 0; i < kRW / 2; ++i) mbar_init(comb_empty0 + 8 * (kRW + i), 2);
+    *reinterpret_cast<volatile int*>(base + S.smem_misc + 68) = 0;
     mbar_init_fence();
   }
   __syncthreads();
@@ -441,84 +553,83 @@ __global__ void __launch_bounds__(kThreads, 1) step_kernel(const __grid_constant
     for (int j = 0; j < S.nops && ok; ++j) {
       const StepOp& op = S.ops[j];
       int64_t ub, ue;
-      step_units(op.a, G, cta, ub, ue);
+      step_units(op.a, cta, ub, ue);
       switch (op.fmt) {
-        case FMT_NV4: ok = step_produce<FMT_NV4>(op.a, ub, ue, base, S.SLOT, S.NS, full0, empty0, s, round, S.err); break;
-        case FMT_W6: ok = step_produce<FMT_W6>(op.a, ub, ue, base, S.SLOT, S.NS, full0, empty0, s, round, S.err); break;
-        case FMT_MX8: ok = step_produce<FMT_MX8>(op.a, ub, ue, base, S.SLOT, S.NS, full0, empty0, s, round, S.err); break;
-        default: ok = step_produce<FMT_W8>(op.a, ub, ue, base, S.SLOT, S.NS, full0, empty0, s, round, S.err); break;
+        case FMT_NV4: ok = step_produce<FMT_NV4>(op.a, ub, ue, base, S.SLOT, S.NS, full0, empty0, s, round, n, S.err); break;
+        case FMT_W6: ok = step_produce<FMT_W6>(op.a, ub, ue, base, S.SLOT, S.NS, full0, empty0, s, round, n, S.err); break;
+        case FMT_MX8: ok = step_produce<FMT_MX8>(op.a, ub, ue, base, S.SLOT, S.NS, full0, empty0, s, round, n, S.err); break;
+        default: ok = step_produce<FMT_W8>(op.a, ub, ue, base, S.SLOT, S.NS, full0, empty0, s, round, n, S.err); break;
       }
-      n += (int)(ue - ub);
-      if ((threadIdx.x & 31) == 0) *reinterpret_cast<volatile int*>(issued) = n;
     }
     asm volatile("cp.async.wait_all;" ::: "memory");
-    if ((threadIdx.x & 31) == 0) *reinterpret_cast<volatile int*>(issued) = ok ? n : -1 - n;
+    // the number of stages issued, marked final (negative) for consumers that stopped early and drain the ring
+    if ((threadIdx.x & 31) == 0) *reinterpret_cast<volatile int*>(issued) = -1 - n;
     return;
   }
 
   // ---------------- consumers ----------------
-  StepConsumerState st{0, 0u, 0u};
-  bool ok = true;
-  int consumed = 0;
+  pdl_wait();  // the first ops read what the previous kernel of the stream wrote
+  StepConsumerState st{0, 0u, 0u, 0u, 0};
+  int* stop = reinterpret_cast<int*>(base + S.smem_misc + 72);
+  bool stopped = false;
   for (int j = 0; j < S.nops; ++j) {
     const StepOp& op = S.ops[j];
     int64_t ub, ue;
-    step_units(op.a, G, cta, ub, ue);
+    step_units(op.a, cta, ub, ue);
+    if (j == S.nops - 1) pdl_launch_dependents();
+    step_stamp(S, j, 0);
     if (ue > ub) {
+      // a warp whose bounded wait gave up has set the error word; every warp still reaches the barriers below
       switch (op.epi * 8 + op.fmt) {
         case EPI_STORE * 8 + FMT_NV4:
-          ok = step_consume<FMT_NV4, NT, EPI_STORE, SHAPE_128x2>(S, op, ub, ue, base, full0, empty0, comb_full0,
-                                                                 comb_empty0, st);
+          step_consume<FMT_NV4, EPI_STORE>(S, op, (int)ub, (int)ue, base, full0, empty0, comb_full0,
+                                                            comb_empty0, st);
           break;
         case EPI_STORE * 8 + FMT_W6:
-          ok = step_consume<FMT_W6, NT, EPI_STORE, SHAPE_128x1>(S, op, ub, ue, base, full0, empty0, comb_full0,
-                                                                comb_empty0, st);
+          step_consume<FMT_W6, EPI_STORE>(S, op, (int)ub, (int)ue, base, full0, empty0, comb_full0,
+                                                           comb_empty0, st);
           break;
         case EPI_STORE * 8 + FMT_MX8:
-          ok = step_consume<FMT_MX8, NT, EPI_STORE, SHAPE_128x2>(S, op, ub, ue, base, full0, empty0, comb_full0,
-                                                                 comb_empty0, st);
+          step_consume<FMT_MX8, EPI_STORE>(S, op, (int)ub, (int)ue, base, full0, empty0, comb_full0,
+                                                            comb_empty0, st);
           break;
         case EPI_HC_DOWN * 8 + FMT_W8:
-          ok = step_consume<FMT_W8, NT, EPI_HC_DOWN, SHAPE_128x2>(S, op, ub, ue, base, full0, empty0, comb_full0,
-                                                                  comb_empty0, st);
+          step_consume<FMT_W8, EPI_HC_DOWN>(S, op, (int)ub, (int)ue, base, full0, empty0, comb_full0,
+                                                             comb_empty0, st);
           break;
         case EPI_HC_UP * 8 + FMT_W8:
-          ok = step_consume<FMT_W8, NT, EPI_HC_UP, SHAPE_128x2>(S, op, ub, ue, base, full0, empty0, comb_full0,
-                                                                comb_empty0, st);
+          step_consume<FMT_W8, EPI_HC_UP>(S, op, (int)ub, (int)ue, base, full0, empty0, comb_full0,
+                                                           comb_empty0, st);
           break;
         default:
-          ok = step_consume<FMT_W8, NT, EPI_STORE, SHAPE_128x2>(S, op, ub, ue, base, full0, empty0, comb_full0,
-                                                                comb_empty0, st);
+          step_consume<FMT_W8, EPI_STORE>(S, op, (int)ub, (int)ue, base, full0, empty0, comb_full0,
+                                                           comb_empty0, st);
           break;
       }
-      consumed += (int)(ue - ub);
     }
-    // the op is finished on this CTA once every consumer warp is past its last flush
+    // the op is finished on this CTA once every consumer warp is past its last flush; one decision for all warps
     named_bar(1, kCWarps * 32);
-    if (!ok || ld_volatile(S.err)) {
-      ok = false;
+    if (threadIdx.x == 0) *reinterpret_cast<volatile int*>(stop) = ld_volatile(S.err) != 0;
+    named_bar(1, kCWarps * 32);
+    if (*reinterpret_cast<volatile int*>(stop)) {
+      stopped = true;
       break;
     }
     if (threadIdx.x == 0) {
       __threadfence();
       atomicAdd(S.done + j, 1);
     }
+    step_stamp(S, j, 3);
   }
-  if (!ok) {
-    // leave no bulk copy in flight: wait (bounded) for every stage the producer issued but nobody consumed
-    if ((threadIdx.x & 31) == 0) {
-      const uint64_t t0 = global_ns();
-      int n;
-      while ((n = *reinterpret_cast<volatile int*>(issued)) >= 0 && global_ns() - t0 < 2000000000ull) {
-        __nanosleep(1000);
-        if (n == consumed) break;
-      }
-    }
-    __syncwarp();
+  if (stopped) {
+    // leave no bulk copy in flight: once the producer has stopped (it notices the error word), wait (bounded) for
+    // every stage it issued that this warp has not taken
+    const uint64_t t0 = global_ns();
+    while (*reinterpret_cast<volatile int*>(issued) >= 0 && global_ns() - t0 < 2000000000ull) __nanosleep(1000);
     const int total = *reinterpret_cast<volatile int*>(issued);
     const int n = total >= 0 ? total : -1 - total;
-    for (int i = consumed; i < n; ++i) {
-      mbar_wait_bounded(full0 + 8 * st.s, st.phase, S.err, 2000000000ull);
+    for (int i = st.consumed; i < n; ++i) {
+      if (!mbar_wait_bounded(full0 + 8 * st.s, st.phase, nullptr, 2000000000ull)) break;
       if (++st.s == S.NS) { st.s = 0; st.phase ^= 1u; }
     }
     return;

@@ -19,6 +19,8 @@ reference's packing bit for bit.
 """
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
 import fp4x_native as N
@@ -779,3 +781,106 @@ class PackedCache:
         save_file(tensors, tmp)
         os.replace(tmp, p)
         return out
+
+
+# ----------------------------------------------------------------------------------------------------------
+# a decode step in one persistent launch (fp4x_step_*)
+# ----------------------------------------------------------------------------------------------------------
+
+class StepProgram:
+    """The GEMV-family ops of a decode step, run as one persistent launch (one CTA per SM).
+
+    Record the ops with the methods below (inputs and outputs are caller-owned tensors that must stay alive), then
+    prepare() once outside graph capture and run() every step.  Each op computes what its standalone entry point
+    computes (the same weights and rounding points; partial sums in a fixed order).  With serial=True every op also
+    waits for the op recorded before it, the order of a single stream; otherwise an op waits only for the earlier
+    ops whose buffers it reads or overwrites.  1..8 tokens."""
+
+    def __init__(self, device, m, serial=True):
+        if not 1 <= m <= 8:
+            raise ValueError("StepProgram runs 1..8 tokens")
+        self.device = torch.device(device)
+        self.m = m
+        self.serial = serial
+        self.ops = []
+        self.keep = []
+        self.table = None
+
+    def _add(self, kind, x, p0, p1, s, out, n, k, gs=1.0, out2=None, out_dtype=torch.bfloat16, lr=0, hc=0, bj=0,
+             nrm=None):
+        if self.table is not None:
+            raise RuntimeError("the step is already prepared")
+        if x.shape[0] != self.m or x.dtype != torch.bfloat16 or x.stride(-1) != 1:
+            raise ValueError(f"activations must be bf16 [{self.m}, k] with unit column stride")
+        self.keep.extend(t for t in (x, p0, p1, s, out, out2, nrm) if t is not None)
+        op = N.StepOpC(kind, x.data_ptr(), x.stride(0), p0.data_ptr(), 0 if p1 is None else p1.data_ptr(),
+                       s.data_ptr(), float(gs), out.data_ptr(), 0 if out2 is None else out2.data_ptr(),
+                       out.stride(0), N.dtype_code(out_dtype), n, k, lr, hc, bj,
+                       0 if nrm is None else nrm.data_ptr(), 0 if nrm is None else nrm.stride(0))
+        self.ops.append(op)
+        return out
+
+    def nv4(self, x, wp, s, gs, out):
+        return self._add(N.STEP_NV4, x, _rows(wp), None, _rows(_u8(s)), out, wp.shape[0], wp.shape[1] * 2, gs=gs,
+                         out_dtype=out.dtype)
+
+    def w6(self, x, L, H, S, out):
+        return self._add(N.STEP_W6, x, _rows(L), _rows(H), _rows(S), out, L.shape[0], L.shape[1] * 2,
+                         out_dtype=out.dtype)
+
+    def w8(self, x, q, s, out):
+        return self._add(N.STEP_W8, x, _rows(q), None, _rows(s.float()), out, q.shape[0], q.shape[1],
+                         out_dtype=out.dtype)
+
+    def mx8(self, x, w8, s, out):
+        return self._add(N.STEP_MX8, x, _rows(_u8(w8)), None, _rows(_u8(s)), out, w8.shape[0], w8.shape[1],
+                         out_dtype=out.dtype)
+
+    def hc_down(self, x, q, s, di, bot, lr, hc):
+        return self._add(N.STEP_HC_DOWN, x, _rows(q), None, _rows(s.float()), di, q.shape[0], q.shape[1], out2=bot,
+                         lr=lr, hc=hc)
+
+    def hc_up(self, bot, qi, si, nrm, out, hc, bj=8):
+        return self._add(N.STEP_HC_UP, bot, _rows(qi), None, _rows(si.float()), out, qi.shape[0], qi.shape[1],
+                         hc=hc, bj=bj, nrm=nrm)
+
+    def prepare(self):
+        arr = (N.StepOpC * len(self.ops))(*self.ops)
+        tb, wb, nc = N._sz(0), N._sz(0), N._i64(0)
+        N.call("fp4x_step_query", arr, len(self.ops), self.m, 1 if self.serial else 0, ctypes.byref(tb),
+               ctypes.byref(wb), ctypes.byref(nc))
+        self.table = torch.empty(tb.value + 64, dtype=torch.uint8, device=self.device)
+        off = (-self.table.data_ptr()) % 64
+        self.table_view = self.table[off:off + tb.value]
+        self.ws = torch.empty(max(wb.value, 16), dtype=torch.uint8, device=self.device)
+        self.cnt = torch.zeros(nc.value, dtype=torch.int32, device=self.device)
+        N.call("fp4x_step_prepare", arr, len(self.ops), self.m, 1 if self.serial else 0, N.ptr(self.table_view),
+               tb.value, N.ptr(self.ws), self.ws.numel(), N.ptr(self.cnt), nc.value)
+        return self
+
+    def run(self):
+        if self.table is None:
+            self.prepare()
+        N.call("fp4x_step_run", N.ptr(self.table_view), N.stream_of(self.table))
+
+    def trace(self, on=True):
+        """Diagnostic: record a [CTAs, ops, 8] timeline on later runs (ns: op start, inputs ready, staged, done,
+        first weight stage ready, stage loop done, last flush done); returns the int64 buffer (read it after the
+        run), or None when turned off."""
+        if self.table is None:
+            self.prepare()
+        if not on:
+            N.call("fp4x_step_trace", N.ptr(self.table_view), None, 0)
+            return None
+        sms = torch.cuda.get_device_properties(self.device).multi_processor_count
+        buf = torch.zeros(sms, len(self.ops), 8, dtype=torch.int64, device=self.device)
+        N.call("fp4x_step_trace", N.ptr(self.table_view), N.ptr(buf), buf.numel())
+        self._trace = buf
+        return buf
+
+    def __del__(self):
+        if getattr(self, "table", None) is not None:
+            try:
+                N.lib().fp4x_step_release(N.ptr(self.table_view))
+            except Exception:  # noqa: BLE001 - interpreter shutdown
+                pass

@@ -37,6 +37,18 @@ class W8Item(ctypes.Structure):
     """fp4x_w8_item of include/fp4x.h."""
     _fields_ = [("x", ctypes.c_void_p), ("q", ctypes.c_void_p), ("s", ctypes.c_void_p), ("out", ctypes.c_void_p)]
 
+class StepOpC(ctypes.Structure):
+    """fp4x_step_op of include/fp4x.h."""
+    _fields_ = [("kind", ctypes.c_int), ("x", ctypes.c_void_p), ("x_stride", ctypes.c_int64),
+                ("p0", ctypes.c_void_p), ("p1", ctypes.c_void_p), ("s", ctypes.c_void_p), ("gs", ctypes.c_float),
+                ("out", ctypes.c_void_p), ("out2", ctypes.c_void_p), ("out_stride", ctypes.c_int64),
+                ("out_dtype", ctypes.c_int), ("n", ctypes.c_int64), ("k", ctypes.c_int64), ("lr", ctypes.c_int64),
+                ("hc", ctypes.c_int64), ("bj", ctypes.c_int64), ("nrm", ctypes.c_void_p),
+                ("nrm_stride", ctypes.c_int64)]
+
+
+STEP_NV4, STEP_W6, STEP_W8, STEP_HC_DOWN, STEP_HC_UP, STEP_MX8 = range(6)
+
 # argument signatures of every exported entry point (must match include/fp4x.h)
 _SIGS = {
     "fp4x_version": ([], _i32),
@@ -73,6 +85,11 @@ _SIGS = {
     "fp4x_draft_head": ([_p, _i64, _p, _p, _i32, _p, _p, _f32, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _i64, _i64,
                          _p, _sz, _p, _i64, _p], _i32),
     "fp4x_head_merge": ([_p, _p, _p, _i64, _i64, _i64, _i64, _p, _p, _p, _p, _p], _i32),
+    "fp4x_step_query": ([_p, _i64, _i64, _i32, ctypes.POINTER(_sz), ctypes.POINTER(_sz), ctypes.POINTER(_i64)], _i32),
+    "fp4x_step_prepare": ([_p, _i64, _i64, _i32, _p, _sz, _p, _sz, _p, _i64], _i32),
+    "fp4x_step_run": ([_p, _p], _i32),
+    "fp4x_step_release": ([_p], _i32),
+    "fp4x_step_trace": ([_p, _p, _i64], _i32),
     "fp4x_quantize_w8": ([_p, _i32, _i64, _i64, _p, _p, _i32, _p], _i32),
     "fp4x_quantize_w6": ([_p, _i32, _i64, _i64, _i32, _p, _p, _p, _i32, _p], _i32),
     "fp4x_amax": ([_p, _i32, _i64, _p, _p], _i32),
