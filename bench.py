@@ -949,6 +949,42 @@ def profile_arm(args):
     return 0
 
 
+def step_trace_arm(args):
+    """Diagnostic: one traced run of the persistent step kernel; prints, per op kind of a layer, the mean time (µs)
+    a CTA waits for the op's inputs, stages them, waits for its first weight stage, runs its stage loop and its
+    last split-K flush, and the op's span over all CTAs (layers 2 to 45)."""
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    step = DecodeStep(dev, args.m, args.layers, 0, 1, step_kernel=True, serial=args.serial)
+    prog = step.prog
+    for _ in range(3):
+        prog.run()
+    torch.cuda.synchronize(dev)
+    tr = prog.trace(True)
+    prog.run()
+    torch.cuda.synchronize(dev)
+    prog.trace(False)
+    t = tr.cpu().numpy().astype(np.int64)
+    names = ("nv4_qkvz", "w6_2560x4096", "w6_4096x2560", "w8_gate", "hc_down", "hc_up")
+    out = {"step_us": round(float(t[:, :, 3].max() - t[:, 0, 0].min()) / 1e3, 1),
+           "order": "single-stream" if args.serial else "buffer hazards"}
+    nops = t.shape[1]
+    for k, name in enumerate(names):
+        cols = {"inputs": [], "staging": [], "first_stage": [], "stage_loop": [], "last_flush": [], "span": []}
+        for j in range(k + 12, nops - 12, 6):
+            st = t[:, j, :]
+            act = st[:, 1] > 0
+            cols["inputs"].append((st[act, 1] - st[act, 0]).mean())
+            cols["staging"].append((st[act, 2] - st[act, 1]).mean())
+            cols["first_stage"].append((st[act, 4] - st[act, 2]).mean())
+            cols["stage_loop"].append((st[act, 5] - st[act, 4]).mean())
+            cols["last_flush"].append((st[act, 6] - st[act, 5]).mean())
+            cols["span"].append(st[:, 3].max() - st[:, 0].min())
+        out[name] = {c: round(float(np.mean(v)) / 1e3, 2) for c, v in cols.items()} | {"ctas": int(act.sum())}
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -963,6 +999,8 @@ def main():
                     help="run the 48 layers as one persistent launch (F.StepProgram) instead of one launch per GEMV")
     ap.add_argument("--dataflow", dest="serial", action="store_false",
                     help="with --step-kernel: order ops by their buffer hazards only (default: single-stream order)")
+    ap.add_argument("--step-trace", action="store_true",
+                    help="diagnostic: one traced run of the persistent step kernel, per-op-kind timeline as JSON")
     ap.add_argument("--kernel-class", default=None,
                     help="profiling aid: launch only these kernel classes (comma list or 'all') and exit")
     ap.add_argument("--launches", type=int, default=3, help="launches per class with --kernel-class")
@@ -975,6 +1013,8 @@ def main():
             ap.error("--gpus N > 1 runs under torchrun (one process per GPU)")
     if args.kernel_class:
         return profile_arm(args)
+    if args.step_trace:
+        return step_trace_arm(args)
     return reference_arm(args) if args.impl == "reference" else native_arm(args)
 
 

@@ -225,10 +225,20 @@ def reset_counters(device=None):
         b.zero_()
 
 
+_queries = {}
+
+
 def query(fmt, m, n, k, batch=1, group=16):
+    """(workspace bytes, counters) of a GEMV-family call; the plan depends on the shape and the device only, so
+    the answer is remembered per (device, shape) and eager calls pay one ctypes round trip per new shape."""
+    key = (torch.cuda.current_device() if torch.cuda.is_available() else -1, fmt, m, n, k, batch, group)
+    hit = _queries.get(key)
+    if hit is not None:
+        return hit
     ws = _sz(0)
     nc = _i64(0)
     call("fp4x_gemv_query", fmt, m, n, k, batch, group, ctypes.byref(ws), ctypes.byref(nc))
+    _queries[key] = (ws.value, nc.value)
     return ws.value, nc.value
 
 
