@@ -985,6 +985,162 @@ def step_trace_arm(args):
     return 0
 
 
+def timeline_arm(args):
+    """Diagnostic: one replay of the captured per-GEMV step with the launch timeline installed; prints, per op of a
+    layer (means over layers 2 to 45, µs, each phase ending at the latest CTA): `hop` = earliest return from the wait
+    for the previous launch minus that launch's last output store, `x_load` = activation rows landed after the wait,
+    `convert` = activations converted after landing, `first_stage` = first weight stage ready after that (negative:
+    it was already resident), `loop` = accumulation done after both, `handover` = the k-groups' sums combined,
+    `reduce` = cross-CTA sums combined, `epilogue` = outputs stored, `total` = last store minus the previous
+    launch's last store; `late_start` = latest CTA start minus the earliest return from the wait (positive: CTAs
+    that could only start once the previous launch left the SM)."""
+    import fp4x_native as N
+    N.use_timeline_library()  # the product library has no stamp sites
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    step = DecodeStep(dev, args.m, args.layers, 0, 1)
+    step.body()
+    torch.cuda.synchronize(dev)
+    tl = N.Timeline(8 * args.layers + 64, dev)
+    s = torch.cuda.Stream(dev)
+    s.wait_stream(torch.cuda.current_stream(dev))
+    g = torch.cuda.CUDAGraph()
+    tl.begin()
+    with torch.cuda.stream(s):
+        with torch.cuda.graph(g, stream=s):
+            h = step.h0
+            for L in step.layers:
+                h = step.layer(L, h)
+    torch.cuda.current_stream(dev).wait_stream(s)
+    n = tl.end()
+    for _ in range(3):
+        g.replay()
+    torch.cuda.synchronize(dev)
+    tl.arm()
+    g.replay()
+    torch.cuda.synchronize(dev)
+    t = tl.read().astype(np.float64)
+    names = ("nv4_qkvz", "w6_2560x4096", "w6_4096x2560", "w8_gate", "hc_down", "hc_up")
+    per = n // args.layers
+    stamps = np.unique(t[:, : N.TL_WAIT_FIRST + 1][t[:, : N.TL_WAIT_FIRST + 1] > 0])
+    gaps = np.diff(stamps)
+    out = {"launches": n, "per_layer": per,
+           "chain_us": round((t[:, N.TL_STORED].max() - t[:, N.TL_START_FIRST].min()) / 1e3, 1),
+           # the globaltimer's update step as seen in the stamps (the resolution of every column below)
+           "timer_step_ns": float(gaps[gaps > 0].min()) if gaps.size else None,
+           "timer_step_ns_median": float(np.median(gaps[gaps > 0])) if gaps.size else None}
+    if per != len(names):
+        out["error"] = "unexpected launches per layer"
+        print(json.dumps(out), flush=True)
+        return 1
+    for k, name in enumerate(names):
+        cols = {c: [] for c in ("hop", "late_start", "x_load", "convert", "first_stage", "loop", "handover", "reduce",
+                                "epilogue", "total")}
+        for j in range(k + 2 * per, n - 2 * per, per):
+            r, pr = t[j], t[j - 1]
+            ready = max(r[N.TL_STAGED], r[N.TL_FIRST_STAGE])
+            hand = r[N.TL_HANDOVER] or r[N.TL_LOOP_DONE]
+            red = r[N.TL_REDUCED] or hand
+            cols["hop"].append(r[N.TL_WAIT_FIRST] - pr[N.TL_STORED])
+            cols["late_start"].append(r[N.TL_START_LAST] - r[N.TL_WAIT_FIRST])
+            cols["x_load"].append(r[N.TL_X_LANDED] - r[N.TL_WAIT_LAST])
+            cols["convert"].append(r[N.TL_STAGED] - r[N.TL_X_LANDED])
+            cols["first_stage"].append(r[N.TL_FIRST_STAGE] - r[N.TL_STAGED])
+            cols["loop"].append(r[N.TL_LOOP_DONE] - ready)
+            cols["handover"].append(hand - r[N.TL_LOOP_DONE])
+            cols["reduce"].append(red - hand)
+            cols["epilogue"].append(r[N.TL_STORED] - red)
+            cols["total"].append(r[N.TL_STORED] - pr[N.TL_STORED])
+        out[name] = {c: round(float(np.mean(v)) / 1e3, 2) for c, v in cols.items()}
+    print(json.dumps(out), flush=True)
+    del g
+    return 0
+
+
+def prefetch_study_arm(args):
+    """Diagnostic: is the per-GEMV layer chain bound by HBM?  Times the 48-layer chain (graph replay, CUDA events):
+    `distinct` = every layer its own weights (the bench workload); `l2_hot` = the first layer's weights 48 times
+    (they stay in the 126 MB L2); `prefetch_op_d` = F.prefetch_l2 of the weights d ops ahead before every op;
+    `prefetch_layer` = the next layer's weights before every layer.  Each variant's final hidden row is compared
+    with the `distinct` one (the prefetch only moves bytes into L2)."""
+    import fp4x_kernels as F
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    step = DecodeStep(dev, args.m, args.layers, 0, 1)
+
+    def tensors(x):
+        return [t for t in (x if isinstance(x, (tuple, list)) else (x,)) if isinstance(t, torch.Tensor)]
+
+    def op_tensors(L):
+        return [tensors(L["nv4"]), tensors(L["w6a"]), tensors(L["w6b"]), tensors(L["gate"]), [L["qd"], L["sd"]],
+                [L["qi"], L["si"]]]
+
+    def chain(layers, d=0, per_layer=False):
+        flat = [ts for L in layers for ts in op_tensors(L)]
+
+        def pf(i):
+            if d and i == 0:
+                for j in range(1, min(d + 1, len(flat))):
+                    F.prefetch_l2(*flat[j])
+            elif d and i + d < len(flat):
+                F.prefetch_l2(*flat[i + d])
+
+        h = step.h0
+        for li, L in enumerate(layers):
+            b = 6 * li
+            if per_layer and li + 1 < len(layers):
+                F.prefetch_l2(*[t for ts in flat[b + 6: b + 12] for t in ts])
+            pf(b)
+            q = F.nv4_linear(h, *L["nv4"])
+            pf(b + 1)
+            o = F.w6_linear(q[:, :W6_IN], *L["w6a"])
+            pf(b + 2)
+            F.w6_linear(o, *L["w6b"])
+            pf(b + 3)
+            F.w8_linear(h, *L["gate"])
+            pf(b + 4)
+            _, bot = step.fx.down(step.streams, L["qd"], L["sd"], LR, HCN)
+            pf(b + 5)
+            h = F.HCFused.up(bot, L["qi"], L["si"], step.streams, HCN, (8, 64, 8))
+        return h
+
+    def timed(fn, reps=20):
+        for _ in range(3):
+            fn()
+        torch.cuda.synchronize(dev)
+        s = torch.cuda.Stream(dev)
+        s.wait_stream(torch.cuda.current_stream(dev))
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(s):
+            with torch.cuda.graph(g, stream=s):
+                out = fn()
+        torch.cuda.current_stream(dev).wait_stream(s)
+        for _ in range(3):
+            g.replay()
+        torch.cuda.synchronize(dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1) / reps
+        out = out.clone()
+        del g
+        return round(ms, 4), out
+
+    res = {}
+    res["distinct_ms"], ref = timed(lambda: chain(step.layers))
+    res["l2_hot_ms"], _ = timed(lambda: chain([step.layers[0]] * len(step.layers)))
+    for d in (1, 2):
+        res[f"prefetch_op_{d}_ms"], out = timed(lambda: chain(step.layers, d=d))
+        res[f"prefetch_op_{d}_same"] = bool(torch.equal(out, ref))
+    res["prefetch_layer_ms"], out = timed(lambda: chain(step.layers, per_layer=True))
+    res["prefetch_layer_same"] = bool(torch.equal(out, ref))
+    print(json.dumps(res), flush=True)
+    return 0
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
@@ -1001,6 +1157,10 @@ def main():
                     help="with --step-kernel: order ops by their buffer hazards only (default: single-stream order)")
     ap.add_argument("--step-trace", action="store_true",
                     help="diagnostic: one traced run of the persistent step kernel, per-op-kind timeline as JSON")
+    ap.add_argument("--prefetch-study", action="store_true",
+                    help="diagnostic: the layer chain with L2-resident weights and with F.prefetch_l2, as JSON")
+    ap.add_argument("--timeline", action="store_true",
+                    help="diagnostic: per-op launch timeline of the per-GEMV step (globaltimer stamps) as JSON")
     ap.add_argument("--kernel-class", default=None,
                     help="profiling aid: launch only these kernel classes (comma list or 'all') and exit")
     ap.add_argument("--launches", type=int, default=3, help="launches per class with --kernel-class")
@@ -1013,6 +1173,10 @@ def main():
             ap.error("--gpus N > 1 runs under torchrun (one process per GPU)")
     if args.kernel_class:
         return profile_arm(args)
+    if args.timeline:
+        return timeline_arm(args)
+    if args.prefetch_study:
+        return prefetch_study_arm(args)
     if args.step_trace:
         return step_trace_arm(args)
     return reference_arm(args) if args.impl == "reference" else native_arm(args)

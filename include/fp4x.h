@@ -344,6 +344,25 @@ int fp4x_nv4_unswizzle_scales(const uint8_t* in, int64_t n, int64_t kb, uint8_t*
 int fp4x_interleave_rows(const void* in, int64_t row_bytes, int64_t n, int64_t hc, int64_t bj, void* out,
                          void* stream);
 
+/* Diagnostic with no reference counterpart: a launch timeline.  While installed, every GEMV launch (register-decode
+ * and tcgen05 kernels) takes the next record of `records` (device memory, `count` records of 16 uint64 words, in
+ * launch order; under stream capture the record is fixed at capture time and rewritten by every replay).  Words
+ * (globaltimer ns, latest over the launch's CTAs unless noted): 0 earliest CTA start, 1 latest CTA start, 2 return
+ * from the wait for the previous launch, 3 activation rows landed in shared memory, 4 activations converted (NVFP4
+ * tensor-core kernel: token maxima known), 5 first weight stage ready, 6 accumulation done, 7 the two k-groups'
+ * sums combined, 8 cross-CTA partial sums combined, 9 outputs stored, 10 earliest return from the wait, 11-15
+ * unused.  Words 7 and 8 stay 0 in the tensor-core kernels.  The caller sets words 0 and 10 to all ones and the
+ * others to zero before the launches run.  fp4x_timeline_end uninstalls the buffer and returns the number of
+ * records handed out. */
+int fp4x_timeline_begin(void* records, int64_t count);
+int64_t fp4x_timeline_end(void);
+
+/* Addition with no reference counterpart: pull up to 16 byte ranges (a later op's packed weights) from HBM into L2
+ * while the stream's current op computes.  Stream-ordered as a programmatic-dependent launch: it releases the next
+ * launch at once and retires only after the stream's previous work, so it adds no wait to the chain.  n = 0 or
+ * zero-sized ranges launch nothing. */
+int fp4x_prefetch_l2(const void* const* ptrs, const int64_t* bytes, int n, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -29,6 +29,37 @@ FP4X_DEV uint64_t global_ns() {
   return t;
 }
 
+// Launch timeline, a diagnostic compiled only into libraries built with FP4X_TIMELINE (the stamp sites, even when
+// not taken, cost the product kernels about 0.3 µs per launch): kTlWords globaltimer words per launch, recorded
+// while the host has installed a buffer (fp4x_timeline_begin).  kTlStartFirst and kTlWaitFirst keep the earliest
+// stamp of their event over the launch's CTAs (atomicMin; the host sets them to all ones), the others the latest
+// (atomicMax; they start at zero).  FP4X_TL(statements) keeps a stamp site in the timeline build only.
+enum TlWord {
+  kTlStartFirst = 0,  // CTA start
+  kTlStartLast,
+  kTlWaitLast,        // return from the wait for the previous launch
+  kTlXLanded,         // activation rows copied into shared memory
+  kTlStaged,          // activations converted (and, NVFP4 on tensor cores, token maxima known)
+  kTlFirstStage,      // first weight stage ready
+  kTlLoopDone,        // accumulation done (consumer thread 0 / the MMA completion)
+  kTlHandover,        // the two k-groups' partial sums combined
+  kTlReduced,         // cross-CTA partial sums combined, epilogue starts
+  kTlStored,          // outputs stored
+  kTlWaitFirst,
+  kTlWords = 16
+};
+#ifdef FP4X_TIMELINE
+#define FP4X_TL(...) __VA_ARGS__
+FP4X_DEV void tl_first(unsigned long long* tl, int i) {
+  if (tl) atomicMin(tl + i, (unsigned long long)global_ns());
+}
+FP4X_DEV void tl_last(unsigned long long* tl, int i) {
+  if (tl) atomicMax(tl + i, (unsigned long long)global_ns());
+}
+#else
+#define FP4X_TL(...)
+#endif
+
 // ------------------------------------------------------------------------------------------------------
 // programmatic dependent launch
 // ------------------------------------------------------------------------------------------------------
@@ -174,6 +205,9 @@ FP4X_DEV uint32_t lds8(uint32_t a) {
 }
 FP4X_DEV void sts64(uint32_t a, uint32_t x, uint32_t y) {
   asm volatile("st.shared.v2.u32 [%0], {%1,%2};" ::"r"(a), "r"(x), "r"(y) : "memory");
+}
+FP4X_DEV void sts16(uint32_t a, uint32_t x) {
+  asm volatile("st.shared.u16 [%0], %1;" ::"r"(a), "h"((unsigned short)x) : "memory");
 }
 
 // ------------------------------------------------------------------------------------------------------

@@ -16,6 +16,17 @@ namespace fp4x {
 __device__ int g_dev_error = 0;
 std::atomic<int64_t> g_launches{0};
 
+// launch timeline (diagnostic): a device buffer of kTlWords words per launch, handed out in launch order
+static std::atomic<unsigned long long*> g_tl_buf{nullptr};
+static std::atomic<int64_t> g_tl_cap{0}, g_tl_next{0};
+
+unsigned long long* timeline_next() {
+  unsigned long long* b = g_tl_buf.load(std::memory_order_acquire);
+  if (!b) return nullptr;
+  const int64_t i = g_tl_next.fetch_add(1, std::memory_order_relaxed);
+  return i < g_tl_cap.load(std::memory_order_relaxed) ? b + kTlWords * i : nullptr;
+}
+
 int* dev_error_ptr() {
   static int* ptrs[64] = {};
   static std::mutex mu;
@@ -408,6 +419,7 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
 // ------------------------------------------------------------------------------------------------------
 static void fill_args(const Plan& pl, GemvArgs& a) {
   a.err = dev_error_ptr();
+  a.tl = timeline_next();
   a.KPW = pl.KPW; a.KP = pl.KP; a.KC = pl.KC; a.NCH = pl.NCH; a.CPP = pl.CPP; a.RT = pl.RT; a.NS = pl.NS;
   a.SMAX = pl.SMAX; a.whole = pl.whole;
   a.BI0 = pl.BI0; a.BI1 = pl.BI1; a.NB0 = pl.NB0; a.SB = pl.SB; a.STG = pl.STG;
@@ -560,6 +572,25 @@ int fp4x_version(void) { return 200; }
 const char* fp4x_last_error_message(void) { return t_msg.c_str(); }
 
 int64_t fp4x_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int fp4x_timeline_begin(void* records, int64_t count) {
+#ifndef FP4X_TIMELINE
+  (void)records;
+  (void)count;
+  return fail(FP4X_ERR_UNSUPPORTED, "built without FP4X_TIMELINE: the timeline is in libfp4x_timeline.so");
+#endif
+  if (!records || count < 1) return fail(FP4X_ERR_INVALID_ARG, "timeline needs a buffer of count >= 1 records");
+  g_tl_cap.store(count, std::memory_order_relaxed);
+  g_tl_next.store(0, std::memory_order_relaxed);
+  g_tl_buf.store((unsigned long long*)records, std::memory_order_release);
+  return FP4X_OK;
+}
+
+int64_t fp4x_timeline_end(void) {
+  g_tl_buf.store(nullptr, std::memory_order_release);
+  const int64_t n = g_tl_next.load(std::memory_order_relaxed), cap = g_tl_cap.load(std::memory_order_relaxed);
+  return n < cap ? n : cap;
+}
 
 int fp4x_device_error(void* stream, int clear, int* code_out) {
   int v = 0;

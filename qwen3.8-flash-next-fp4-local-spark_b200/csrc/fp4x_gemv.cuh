@@ -111,6 +111,7 @@ struct alignas(64) GemvArgs {
   int* sem;               // arrival counters [batch * RT * 4], zero on entry and on exit
   int* err;               // device error word
   int xdirect;            // 1: no raw panel in shared memory; staging reads the activations from global memory
+  unsigned long long* tl;  // launch timeline record (diagnostic) or null
 };
 
 // ------------------------------------------------------------------------------------------------------
@@ -324,6 +325,7 @@ FP4X_DEV void stage_activations(const GemvArgs& A, const GemvItem& it, uint8_t* 
       bulk_g2s(smem_u32(base + A.smem_xraw) + m * bytes, x + (int64_t)m * A.x_stride + k_panel0, bytes, xbar);
   }
   if (!mbar_wait_bounded(xbar, 0, A.err)) return;
+  FP4X_TL(if (tid == 0) tl_last(A.tl, kTlXLanded));
   if (G.xf16) {
     for (int tok = warp; tok < MP; tok += kCWarps) {
       float mx = 0.f;
@@ -961,6 +963,7 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
   const int64_t nunits = u_end - u_begin;
 
   if (threadIdx.x == 0) {
+    FP4X_TL(tl_first(A.tl, kTlStartFirst); tl_last(A.tl, kTlStartLast));  // timeline: CTA start
     for (int s = 0; s < A.NS; ++s) {
       mbar_init(full0 + 8 * s, 33);
       mbar_init(empty0 + 8 * s, kCWarps);
@@ -1029,9 +1032,11 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
   const int g = lane >> 2, tq = lane & 3;
   const int wrow = warp & (kRW - 1), kg = warp / kRW;
   pdl_wait();
+  FP4X_TL(if (threadIdx.x == 0) { tl_last(A.tl, kTlWaitLast); tl_first(A.tl, kTlWaitFirst); });
   stage_activations<FMT, NT>(A, it, base, MP, k_panel0, xbar);
   named_bar(1, kCWarps * 32);
   pdl_launch_dependents();
+  FP4X_TL(if (threadIdx.x == 0) tl_last(A.tl, kTlStaged));
 
   const float* xsc = reinterpret_cast<const float*>(base + A.smem_misc);
   float* scr = reinterpret_cast<float*>(base + A.smem_scr);
@@ -1078,6 +1083,7 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(ce_bar);
+    FP4X_TL(if (lane == 0) tl_last(A.tl, kTlHandover));
     if (G.xf16) {
 #pragma unroll
       for (int t = 0; t < NT; ++t)
@@ -1121,6 +1127,7 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
           tot[t][0] += v.x; tot[t][1] += v.y; tot[t][2] += v.z; tot[t][3] += v.w;
         }
       }
+      FP4X_TL(if (lane == 0) tl_last(A.tl, kTlReduced));
       run_epilogue<EPI, NT>(A, it, row0, tot, wrow, g, tq, scr);
       return;
     }
@@ -1134,6 +1141,7 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
     }
     const int segs = cl - cf + 1;
     if (A.KP == 1 && segs == 1) {
+      FP4X_TL(if (lane == 0) tl_last(A.tl, kTlReduced));
       run_epilogue<EPI, NT>(A, it, row0, acc, wrow, g, tq, scr);
       return;
     }
@@ -1196,10 +1204,14 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
         }
       }
     }
+    FP4X_TL(if (lane == 0) tl_last(A.tl, kTlReduced));
     run_epilogue<EPI, NT>(A, it, row0, tot, wrow, g, tq, scr);
     if (lane == 0) atomicExch(semp, 0);
   };
 
+  // timeline: first weight stage resident (a wait on phase 0 of stage 0 consumes nothing; only while recording)
+  FP4X_TL(if (A.tl && threadIdx.x == 0 && nunits > 0 && mbar_wait_bounded(full0, 0, A.err))
+              tl_last(A.tl, kTlFirstStage));
   int s = 0;
   uint32_t phase = 0;
   int blk = (int)(u_begin / A.NCH), chunk = (int)(u_begin - (int64_t)blk * A.NCH);
@@ -1221,7 +1233,9 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
     if (++s == A.NS) { s = 0; phase ^= 1u; }
     if (++chunk == A.NCH) { chunk = 0; ++blk; }
   }
+  FP4X_TL(if (threadIdx.x == 0) tl_last(A.tl, kTlLoopDone));
   if (ok && cur >= 0) flush(cur);
+  FP4X_TL(if (lane == 0) tl_last(A.tl, kTlStored));
 }
 
 // Two entry points with one body.  Plans with more CTAs than SMs keep two CTAs per SM (at most ~100 registers per

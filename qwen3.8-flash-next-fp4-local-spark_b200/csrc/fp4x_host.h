@@ -23,6 +23,8 @@ const DeviceFacts& device_facts();
 
 // kernels launched (or recorded into a graph under capture) by this library; read by fp4x_launch_count
 extern std::atomic<int64_t> g_launches;
+// the timeline record of the next launch (kTlWords words), or null when no timeline buffer is installed / it is full
+unsigned long long* timeline_next();
 
 // launch with programmatic stream serialization (the kernel may begin while its predecessor drains)
 template <typename Kernel, typename... Args>

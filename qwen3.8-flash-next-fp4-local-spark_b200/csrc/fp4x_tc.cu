@@ -64,6 +64,7 @@ int run_nv4_tc(const void* x, int64_t x_stride, const void* wp, const void* sc, 
   a.out = out; a.out_stride = out_stride; a.out_dtype = out_dtype; a.gs = gs;
   a.M = (int)m; a.N = (int)n; a.K = (int)k; a.NB = NB;
   a.err = dev_error_ptr();
+  a.tl = timeline_next();
   const unsigned grid = (unsigned)((n + tc::kRows - 1) / tc::kRows);
   switch (m) {
     case 1: return launch_nv4_tc<1>(a, grid, smem_total, stream);
@@ -125,6 +126,7 @@ int run_mx8_tc(const void* x, int64_t x_stride, const void* w, const void* sc, v
   a.out = out; a.out_stride = out_stride; a.out_dtype = out_dtype;
   a.M = (int)m; a.N = (int)n; a.K = (int)k;
   a.err = dev_error_ptr();
+  a.tl = timeline_next();
   const unsigned grid = (unsigned)((n + tc::kRows - 1) / tc::kRows);
   switch (m) {
     case 1: return launch_mx8_tc<1>(a, grid, smem_total, stream);
@@ -172,6 +174,7 @@ int run_int2_tc(const void* x, int64_t x_stride, const void* p, const void* s, i
   a.M = (int)m; a.N = (int)n; a.K = (int)k; a.group = group;
   a.tiles = (int)((n + tc::kRows - 1) / tc::kRows);
   a.err = dev_error_ptr();
+  a.tl = timeline_next();
   const unsigned grid = (unsigned)std::min(a.tiles, dv.sms);
   auto kern = tc::int2_tc_kernel;
   cudaError_t e = ensure_smem_attr((const void*)kern, smem_total);

@@ -70,6 +70,7 @@ struct Args {
   int NS;                     // stages
   int smem_b, smem_xraw, smem_sfb, smem_misc;
   int* err;
+  unsigned long long* tl;  // launch timeline record (diagnostic builds) or null
 };
 
 // ---- tensor-core primitives ----
@@ -226,6 +227,7 @@ __global__ void __launch_bounds__(nv_threads(MT), 1) nv4_tc_kernel(const __grid_
   uint32_t* amax_bits = tmem_slot + 1;  // [kMaxM] max |x| per token (float bits)
 
   if (threadIdx.x == 0) {
+    FP4X_TL(tl_first(A.tl, kTlStartFirst); tl_last(A.tl, kTlStartLast));
     for (int s = 0; s < A.NS; ++s) {
       mbar_init(full0 + 8 * s, 1);
       mbar_init(empty0 + 8 * s, 1);
@@ -275,6 +277,7 @@ __global__ void __launch_bounds__(nv_threads(MT), 1) nv4_tc_kernel(const __grid_
         const int s = st % A.NS;
         // the scale writers have seen this stage's tiles land and this slab's terms done
         if (!mbar_wait_bounded(sfr0 + 8 * st, 0, A.err)) { ok = false; break; }
+        FP4X_TL(if (st == 0) tl_last(A.tl, kTlFirstStage));
         tc_fence_after();
         const uint32_t astage = smem_u32(base) + (uint32_t)s * kStageBytes;
 #pragma unroll
@@ -328,6 +331,7 @@ __global__ void __launch_bounds__(nv_threads(MT), 1) nv4_tc_kernel(const __grid_
     }
     // ---------------- epilogue: row 32 sub + lane of the block, all B columns ----------------
     if (ok && !mbar_wait_bounded(dfull, 0, A.err)) ok = false;
+    FP4X_TL(if (sub == 0 && lane == 0) tl_last(A.tl, kTlLoopDone));
     tc_fence_after();
     if (ok) {
       float d[NBT];
@@ -359,12 +363,14 @@ __global__ void __launch_bounds__(nv_threads(MT), 1) nv4_tc_kernel(const __grid_
           store_out(A.out, A.out_dtype, (int64_t)m * A.out_stride + row, acc * A.gs);
         }
       }
+      FP4X_TL(if (lane == 0) tl_last(A.tl, kTlStored));
     }
     tc_fence_before();
   } else {
     // ---------------- activations -> e2m1 terms (warps 2..7, 12..), slab by slab ----------------
     const int ptid = warp < 8 ? threadIdx.x - 64 : threadIdx.x - 192, pthreads = 192 + 32 * nv_prep_extra(MT);
     pdl_wait();
+    FP4X_TL(if (ptid == 0) { tl_last(A.tl, kTlWaitLast); tl_first(A.tl, kTlWaitFirst); });
     const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(base + A.smem_xraw);
     if (ptid == 0) {
       const uint32_t bytes = (uint32_t)A.K * 2u;
@@ -373,6 +379,7 @@ __global__ void __launch_bounds__(nv_threads(MT), 1) nv4_tc_kernel(const __grid_
         bulk_g2s(smem_u32(base + A.smem_xraw) + m * bytes, A.x + (int64_t)m * A.x_stride, bytes, xbar);
     }
     if (!mbar_wait_bounded(xbar, 0, A.err)) ok = false;
+    FP4X_TL(if (ptid == 0) tl_last(A.tl, kTlXLanded));
     if (ok) {
       for (int m = 0; m < MT; ++m) {
         uint32_t mx = 0;
@@ -391,6 +398,7 @@ __global__ void __launch_bounds__(nv_threads(MT), 1) nv4_tc_kernel(const __grid_
       }
     }
     named_bar(1, pthreads);
+    FP4X_TL(if (ptid == 0) tl_last(A.tl, kTlStaged));
     // blocks in slab-major order (slab, token, block of the slab), so the first slabs are done first
     uint8_t* bsm = base + A.smem_b;
     uint8_t* sfb = base + A.smem_sfb;
@@ -463,6 +471,7 @@ struct MxArgs {
   int NS;
   int smem_b, smem_xraw, smem_sfb, smem_sfa, smem_misc;
   int* err;
+  unsigned long long* tl;  // launch timeline record (diagnostic builds) or null
 };
 
 FP4X_DEV uint32_t idesc_mxf8(int nb, uint32_t sf_id) {

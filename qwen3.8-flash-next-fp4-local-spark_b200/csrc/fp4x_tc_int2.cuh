@@ -73,6 +73,7 @@ struct I2Args {
   int NS;
   int smem_b, smem_misc;
   int* err;
+  unsigned long long* tl;  // launch timeline record (diagnostic) or null
 };
 
 FP4X_DEV uint32_t idesc_bf16_n16() {

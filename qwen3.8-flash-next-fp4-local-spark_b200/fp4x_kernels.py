@@ -617,6 +617,24 @@ def _prep_input(w):
     return w, codes[w.dtype]
 
 
+def prefetch_l2(*tensors):
+    """Pull the tensors' bytes (a later op's packed weights and scales) from HBM into L2 on the current stream
+    (fp4x_prefetch_l2).  Not part of the reference API: a decode step issues it one op ahead so the dependent GEMV
+    chain reads its weights from L2 while HBM keeps streaming.  At most 16 tensors per call."""
+    ts = [t for t in tensors if t is not None and t.numel() > 0]
+    if not ts:
+        return
+    for t in ts:
+        if not t.is_cuda:
+            raise ValueError("prefetch_l2 takes CUDA tensors")
+    ptrs = (ctypes.c_void_p * len(ts))(*[t.data_ptr() for t in ts])
+    # the span from the first to the last element (the whole tensor when it is contiguous)
+    spans = [(sum((n - 1) * st for n, st in zip(t.shape, t.stride())) + 1) * t.element_size() for t in ts]
+    sizes = (ctypes.c_int64 * len(ts))(*spans)
+    N.call("fp4x_prefetch_l2", ctypes.cast(ptrs, ctypes.c_void_p), ctypes.cast(sizes, ctypes.c_void_p), len(ts),
+           N.stream_of(ts[0]))
+
+
 def _interleave_native(t, hc, bj):
     t = t.contiguous()
     n = t.shape[0]

@@ -13,10 +13,13 @@ import ctypes
 import os
 import threading
 
+import numpy as np
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.environ.get("FP4X_LIB", os.path.join(_HERE, "libfp4x.so"))
+# the diagnostic twin with the launch-timeline stamps compiled in (build_native.py --timeline)
+TIMELINE_LIB_PATH = os.path.join(_HERE, "libfp4x_timeline.so")
 
 OK = 0
 ERR_INVALID_ARG, ERR_UNSUPPORTED, ERR_WORKSPACE, ERR_CUDA, ERR_DEVICE = -1, -2, -3, -4, -5
@@ -100,6 +103,9 @@ _SIGS = {
     "fp4x_dequant_int2": ([_p, _p, _i32, _i64, _i64, _p, _p], _i32),
     "fp4x_nv4_unswizzle_scales": ([_p, _i64, _i64, _p, _p], _i32),
     "fp4x_interleave_rows": ([_p, _i64, _i64, _i64, _i64, _p, _p], _i32),
+    "fp4x_prefetch_l2": ([_p, _p, _i32, _p], _i32),
+    "fp4x_timeline_begin": ([_p, _i64], _i32),
+    "fp4x_timeline_end": ([], _i64),
 }
 
 _lib = None
@@ -273,6 +279,50 @@ def plan(fmt, m, n, k, batch=1, group=16, whole=False):
     buf = ctypes.create_string_buffer(512)
     call("fp4x_plan_describe", fmt, m, n, k, batch, group, 1 if whole else 0, buf, 512)
     return buf.value.decode()
+
+
+# launch timeline words (TlWord in csrc/fp4x_common.cuh)
+(TL_START_FIRST, TL_START_LAST, TL_WAIT_LAST, TL_X_LANDED, TL_STAGED, TL_FIRST_STAGE, TL_LOOP_DONE, TL_HANDOVER,
+ TL_REDUCED, TL_STORED, TL_WAIT_FIRST) = range(11)
+
+
+def use_timeline_library():
+    """Load the diagnostic twin (libfp4x_timeline.so) instead of libfp4x.so; must run before the first library call
+    of the process."""
+    global LIB_PATH
+    if _lib is not None and LIB_PATH != TIMELINE_LIB_PATH:
+        raise RuntimeError("libfp4x.so is already loaded in this process")
+    LIB_PATH = TIMELINE_LIB_PATH
+
+
+class Timeline:
+    """Diagnostic launch timeline (fp4x_timeline_begin / fp4x_timeline_end; needs the timeline library, see
+    use_timeline_library): `begin()`, launch or capture the GEMVs,
+    `end()`; then `arm()` before a run (or graph replay) and `read()` after it: a uint64 array [launches, 16] of
+    globaltimer stamps, the words named by the TL_* constants (latest over the launch's CTAs, earliest for the
+    *_FIRST words; TL_HANDOVER and TL_REDUCED stay 0 in the tensor-core kernels)."""
+
+    WORDS = 16
+
+    def __init__(self, count, device):
+        self.buf = torch.zeros(count, self.WORDS, dtype=torch.int64, device=device)
+        self.n = 0
+
+    def begin(self):
+        self.arm()
+        call("fp4x_timeline_begin", ptr(self.buf), self.buf.shape[0])
+
+    def end(self):
+        self.n = int(lib().fp4x_timeline_end())
+        return self.n
+
+    def arm(self):
+        self.buf.zero_()
+        self.buf[:, TL_START_FIRST] = -1  # all ones: the minimum words
+        self.buf[:, TL_WAIT_FIRST] = -1
+
+    def read(self):
+        return self.buf[: self.n].cpu().numpy().view(np.uint64)
 
 
 def launch_count():

@@ -33,6 +33,27 @@ def nv4_weights():
     return P, S, gs, O.nv4_weights(P.numpy(), S.view(torch.uint8).numpy()).astype(np.float64)
 
 
+@pytest.fixture(scope="module")
+def nv4_weights_16384():
+    g = torch.Generator().manual_seed(32)
+    w = torch.randn(16384, K, generator=g) * 0.02  # 128 row tiles: the activation terms are shared by clusters
+    P, S, gs = F.quantize_nv4(w)
+    return P, S, gs, O.nv4_weights(P.numpy(), S.view(torch.uint8).numpy()).astype(np.float64)
+
+
+@pytest.mark.parametrize("m", range(1, 9))
+def test_nv4_tc_clustered_terms_match_oracle(nv4_weights_16384, m):
+    """16384 rows (the C2 / C5 shape): 128 CTAs in clusters that prepare the activation terms once per cluster."""
+    P, S, gs, wdeq = nv4_weights_16384
+    g = torch.Generator().manual_seed(400 + m)
+    x = torch.randn(m, K, generator=g).to(torch.bfloat16)
+    ref = (x.double().numpy() @ wdeq.T) * np.float64(np.float32(gs))
+    Pd, Sd, xd = P.to(DEV), S.to(DEV), x.to(DEV)
+    y32 = F.nv4_linear(xd, Pd, Sd, gs, out_dtype=torch.float32).cpu()
+    assert rel_err(y32, ref) < 2e-4
+    assert torch.equal(F.nv4_linear(xd, Pd, Sd, gs, out_dtype=torch.float32).cpu(), y32)
+
+
 @pytest.mark.parametrize("m", range(1, 9))
 def test_nv4_tc_matches_oracle(nv4_weights, m):
     P, S, gs, wdeq = nv4_weights
