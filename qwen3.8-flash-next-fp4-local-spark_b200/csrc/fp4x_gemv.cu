@@ -262,7 +262,7 @@ static bool make_cluster_plan(int fmt, int64_t M, int64_t N, int64_t K, int grou
     c.XP = (kpw / 16) * 32 + 32;
     const int red_bytes = (KP - 1) * kRW * 32 * c.NT * 16;
     c.xdirect = 0;
-    const int raw = (int)M * kpw * 2;
+    const int raw = fmt == FMT_W8 ? 0 : (int)M * kpw * 2;  // W8 stages into the operand panel directly
     const int xbytes = round_up(c.MP * c.XP, 16) + raw;
     const int fixed = xbytes + misc + comb_bytes + red_bytes + 1024;
     const int ctas = base.RT * KP;
@@ -347,7 +347,8 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
     c.STG = round_up(c.off_sc + kRB * c.SB, 1024);
     c.XP = (kpw / 16) * 32 + 32;
     c.xdirect = direct;
-    const int xbytes = round_up(c.MP * c.XP, 16) + (c.xdirect ? 0 : (int)M * kpw * 2);  // permuted + raw panels
+    // operand panel + raw panel (W8 copies the rows straight into the operand panel: no raw panel)
+    const int xbytes = round_up(c.MP * c.XP, 16) + (c.xdirect || fmt == FMT_W8 ? 0 : (int)M * kpw * 2);
     const int fixed = xbytes + misc + scr_bytes + comb_bytes + 1024;
     for (int cps = 2; cps >= 1; --cps) {
       const int cap = cps == 2 ? cap2 : cap1;
@@ -391,7 +392,7 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
   pl.smem_misc = pl.smem_x + round_up(pl.MP * pl.XP, 16);
   pl.smem_scr = pl.smem_misc + misc;
   pl.smem_xraw = pl.smem_scr + round_up(scr_bytes, 16);
-  pl.smem_comb = pl.smem_xraw + round_up(pl.xdirect ? 0 : (int)M * pl.KPW * 2, 16);
+  pl.smem_comb = pl.smem_xraw + round_up(pl.xdirect || fmt == FMT_W8 ? 0 : (int)M * pl.KPW * 2, 16);
   pl.smem_total = pl.smem_comb + comb_bytes + 1024;
   pl.SMAX = whole ? 1 : (int)((int64_t)(pl.NCH - 1) * pl.CPP / Up) + 2;
   if (pl.SMAX > pl.CPP) pl.SMAX = pl.CPP;

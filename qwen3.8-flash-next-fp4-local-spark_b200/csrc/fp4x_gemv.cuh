@@ -303,6 +303,22 @@ FP4X_DEV void stage_convert(const GemvArgs& A, uint8_t* base, int MP, const __nv
 template <int FMT, int NT>
 FP4X_DEV void stage_activations(const GemvArgs& A, const GemvItem& it, uint8_t* base, int MP, int k_panel0,
                                 uint32_t xbar) {
+  if constexpr (FMT == FMT_W8) {
+    // W8 reads bf16 activations in their own order (stage_block_positions is the identity: block kb at byte 8 kb),
+    // so the operand panel is the raw token rows at the padded pitch XP: the bulk copies land there directly and
+    // nothing is converted
+    if (threadIdx.x == 0) {
+      const uint32_t bytes = (uint32_t)A.KPW * 2u;
+      mbar_arrive_expect_tx(xbar, bytes * (uint32_t)A.M);
+      const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(it.x);
+      for (int m = 0; m < A.M; ++m)
+        bulk_g2s(smem_u32(base + A.smem_x) + m * A.XP, x + (int64_t)m * A.x_stride + k_panel0, bytes, xbar);
+    }
+    const bool landed = mbar_wait_bounded(xbar, 0, A.err);
+    FP4X_TL(if (landed && threadIdx.x == 0) tl_last(A.tl, kTlXLanded));
+    (void)landed;
+    return;
+  }
   // 16-token plans may leave the raw panel in global memory (the flag is compiled into those kernels only)
   if constexpr (NT == 2) {
     if (A.xdirect) {
@@ -859,6 +875,24 @@ FP4X_DEV float hc_gate_mean(const float* nrm_vals, const float* gates, int hc) {
   return bf16_round(p[0] / (float)hc);
 }
 
+// HC up: pull the normalized-stream values that the epilogue of row block `blk` reads (the same indices as
+// run_epilogue's gate-mean loop, for row warp `wrow`) into L1 while the block's stages stream.  The epilogue runs
+// after the reduction, where these loads would otherwise wait a full L2 round trip.
+FP4X_DEV void hc_up_prefetch_nrm(const GemvArgs& A, int blk, int wrow, int lane) {
+  const int rows = A.hc * A.bj;
+  const int first = rows == 32 ? (wrow & ~1) : wrow, nw = rows == 32 ? 2 : 1;
+  const int blk_row0 = blk * kRB + 16 * first;
+  if (blk_row0 >= A.N) return;
+  const int jb = blk_row0 / rows, H = A.N / A.hc;
+  const __nv_bfloat16* nrm = reinterpret_cast<const __nv_bfloat16*>(A.nrm);
+  const int nout = A.bj * A.M;
+  for (int o = lane + 32 * (wrow - first); o < nout; o += 32 * nw) {
+    const int m = o / A.bj, col = jb * A.bj + (o - m * A.bj);
+    for (int sidx = 0; sidx < A.hc; ++sidx)
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(nrm + (int64_t)m * A.nrm_stride + sidx * H + col));
+  }
+}
+
 template <int EPI, int NT>
 FP4X_DEV void run_epilogue(const GemvArgs& A, const GemvItem& it, int row0, const float (&v)[NT][4], int warp, int g,
                            int tq, float* scr_all) {
@@ -1220,6 +1254,9 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
       if (cur >= 0) flush(cur);
       zero4<NT>(acc);
       cur = blk;
+      if constexpr (EPI == EPI_HC_UP) {
+        if (kg == 0) hc_up_prefetch_nrm(A, blk, wrow, lane);
+      }
     }
     if (!mbar_wait_bounded(full0 + 8 * s, phase, A.err)) { ok = false; break; }
     const uint32_t stage = smem_u32(base) + (uint32_t)s * A.STG;
