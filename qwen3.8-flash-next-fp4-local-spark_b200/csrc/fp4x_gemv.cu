@@ -236,19 +236,6 @@ static bool chunk_for(int fmt, int kpw, int& KC, int& BI0, int& NB0) {
   return false;
 }
 
-// Four k-groups (gemv_kernel_kg4) for W8 / W6 plans whose CTAs have an SM each and whose stages are two 128-byte
-// boxes; FP4X_MAX_KG=2 in the environment keeps two (for comparisons).
-static bool kg4_allowed() {
-  static const bool ok = [] {
-    const char* e = getenv("FP4X_MAX_KG");
-    return !(e && atoi(e) < 4);
-  }();
-  return ok;
-}
-static int k_groups(int fmt, bool one_per_sm, int BI0, int NB0) {
-  return (kg4_allowed() && one_per_sm && (fmt == FMT_W8 || fmt == FMT_W6) && BI0 == 128 && NB0 == 2) ? 4 : 2;
-}
-
 // Cluster plan: one row block per CTA, K split into KP panels (2..8) whose CTAs form a (1, KP, 1) cluster; the
 // panel partials are summed in the leader's shared memory.  Picks the largest KP with RT * KP <= 2 * SMs whose panel
 // width has a valid stage shape.  `base` carries the shape fields (NT, MP, RT).
@@ -277,9 +264,8 @@ static bool make_cluster_plan(int fmt, int64_t M, int64_t N, int64_t K, int grou
     c.xdirect = 0;
     const int raw = fmt == FMT_W8 ? 0 : (int)M * kpw * 2;  // W8 stages into the operand panel directly
     const int xbytes = round_up(c.MP * c.XP, 16) + raw;
+    const int fixed = xbytes + misc + comb_bytes + red_bytes + 1024;
     const int ctas = base.RT * KP;
-    c.KG = k_groups(fmt, ctas <= dv.sms, BI0, NB0);
-    const int fixed = xbytes + misc + comb_bytes * (c.KG - 1) + red_bytes + 1024;
     const int cap = ctas > dv.sms ? dv.smem_sm / 2 - 2048 : dv.smem_optin;
     int ns = (cap - fixed) / c.STG;
     if (ns > kMaxStages) ns = kMaxStages;
@@ -294,7 +280,7 @@ static bool make_cluster_plan(int fmt, int64_t M, int64_t N, int64_t K, int grou
     c.smem_scr = c.smem_misc + misc;
     c.smem_xraw = c.smem_scr;
     c.smem_comb = c.smem_xraw + round_up(raw, 16);
-    c.smem_red = c.smem_comb + comb_bytes * (c.KG - 1);
+    c.smem_red = c.smem_comb + comb_bytes;
     c.smem_total = c.smem_red + red_bytes + 1024;
     c.ws_bytes = 0;
     c.counters = 0;
@@ -318,7 +304,6 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
     return fail(FP4X_ERR_UNSUPPORTED, "K=" + std::to_string(K) + " must be a multiple of " + std::to_string(kmin > 64 ? kmin : 64));
   const DeviceFacts& dv = device_facts();
   pl.NT = M <= 8 ? 1 : 2;
-  pl.KG = 2;
   pl.MP = 8 * pl.NT;
   pl.RT = (int)((N + kRB - 1) / kRB);
   // INT2 heads always use whole row blocks: each row's fp32 sum then has a fixed order that does not depend on the
@@ -367,8 +352,7 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
     const int fixed = xbytes + misc + scr_bytes + comb_bytes + 1024;
     for (int cps = 2; cps >= 1; --cps) {
       const int cap = cps == 2 ? cap2 : cap1;
-      const int kgc = k_groups(fmt, cps == 1, BI0, NB0);
-      int ns = (cap - fixed - comb_bytes * (kgc - 2)) / c.STG;
+      int ns = (cap - fixed) / c.STG;
       if (ns > kMaxStages) ns = kMaxStages;
       if (ns < 2 || (cps == 2 && ns < 3)) continue;
       const double inflight = (double)cps * ns * c.STG;
@@ -384,7 +368,6 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
       if (score > best_score) {
         best_score = score;
         c.NS = ns;
-        c.KG = kgc;
         c.CPP = cps;  // CTAs per SM for now
         best_d = c;
         found_d = true;
@@ -410,7 +393,7 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
   pl.smem_scr = pl.smem_misc + misc;
   pl.smem_xraw = pl.smem_scr + round_up(scr_bytes, 16);
   pl.smem_comb = pl.smem_xraw + round_up(pl.xdirect || fmt == FMT_W8 ? 0 : (int)M * pl.KPW * 2, 16);
-  pl.smem_total = pl.smem_comb + comb_bytes * (pl.KG - 1) + 1024;
+  pl.smem_total = pl.smem_comb + comb_bytes + 1024;
   pl.SMAX = whole ? 1 : (int)((int64_t)(pl.NCH - 1) * pl.CPP / Up) + 2;
   if (pl.SMAX > pl.CPP) pl.SMAX = pl.CPP;
   const size_t slot = (size_t)kRW * 16 * pl.MP * sizeof(float);
@@ -657,9 +640,9 @@ int fp4x_plan_describe(int fmt, int64_t m, int64_t n, int64_t k, int64_t batch, 
   if (rc) return rc;
   snprintf(buf, len,
            "KPW=%d KP=%d KC=%d NCH=%d CPP=%d RT=%d NS=%d STG=%d BI0=%d NB0=%d BI1=%d SB=%d smem=%d whole=%d "
-           "ws=%zu counters=%lld ctas=%lld KG=%d",
+           "ws=%zu counters=%lld ctas=%lld",
            pl.KPW, pl.KP, pl.KC, pl.NCH, pl.CPP, pl.RT, pl.NS, pl.STG, pl.BI0, pl.NB0, pl.BI1, pl.SB, pl.smem_total,
-           pl.whole, pl.ws_bytes, (long long)pl.counters, (long long)pl.CPP * pl.KP * batch, pl.KG);
+           pl.whole, pl.ws_bytes, (long long)pl.counters, (long long)pl.CPP * pl.KP * batch);
   return FP4X_OK;
 }
 

@@ -209,15 +209,15 @@ FP4X_DEV uint32_t pick2(uint32_t lo_src, int lo_idx, uint32_t hi_src, int hi_idx
 // 16-token plans whose raw panel would not fit in shared memory beside the converted panel and the weight stages.
 // The shared-memory path in stage_activations keeps its own copy of the same passes: routing it through this
 // function changed the code of the M <= 8 kernels and cost 0.5-1% of the decode step (measured).
-template <int FMT, int CW = kCWarps>
+template <int FMT>
 FP4X_DEV void stage_convert(const GemvArgs& A, uint8_t* base, int MP, const __nv_bfloat16* xr, int64_t xrs) {
   constexpr FmtGeom G = fmt_geom(FMT);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  constexpr int nthr = CW * 32;
+  constexpr int nthr = kCWarps * 32;
   float* xsc = reinterpret_cast<float*>(base + A.smem_misc);  // [MP] scale, [MP] inverse
   const int KPW = A.KPW;
   if (G.xf16) {
-    for (int tok = warp; tok < MP; tok += CW) {
+    for (int tok = warp; tok < MP; tok += kCWarps) {
       float mx = 0.f;
       if (tok < A.M) {
         const uint4* row = reinterpret_cast<const uint4*>(xr + (int64_t)tok * xrs);
@@ -300,8 +300,7 @@ FP4X_DEV void stage_convert(const GemvArgs& A, uint8_t* base, int MP, const __nv
   }
 }
 
-// CW: consumer warps of the CTA (all of them stage)
-template <int FMT, int NT, int CW = kCWarps>
+template <int FMT, int NT>
 FP4X_DEV void stage_activations(const GemvArgs& A, const GemvItem& it, uint8_t* base, int MP, int k_panel0,
                                 uint32_t xbar) {
   if constexpr (FMT == FMT_W8) {
@@ -323,13 +322,13 @@ FP4X_DEV void stage_activations(const GemvArgs& A, const GemvItem& it, uint8_t* 
   // 16-token plans may leave the raw panel in global memory (the flag is compiled into those kernels only)
   if constexpr (NT == 2) {
     if (A.xdirect) {
-      stage_convert<FMT, CW>(A, base, MP, reinterpret_cast<const __nv_bfloat16*>(it.x) + k_panel0, A.x_stride);
+      stage_convert<FMT>(A, base, MP, reinterpret_cast<const __nv_bfloat16*>(it.x) + k_panel0, A.x_stride);
       return;
     }
   }
   constexpr FmtGeom G = fmt_geom(FMT);
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  constexpr int nthr = CW * 32;
+  constexpr int nthr = kCWarps * 32;
   float* xsc = reinterpret_cast<float*>(base + A.smem_misc);  // [MP] scale, [MP] inverse
   const int KPW = A.KPW;
   // one bulk copy per token row brings the raw panel into shared memory in a single round trip
@@ -344,7 +343,7 @@ FP4X_DEV void stage_activations(const GemvArgs& A, const GemvItem& it, uint8_t* 
   if (!mbar_wait_bounded(xbar, 0, A.err)) return;
   FP4X_TL(if (tid == 0) tl_last(A.tl, kTlXLanded));
   if (G.xf16) {
-    for (int tok = warp; tok < MP; tok += CW) {
+    for (int tok = warp; tok < MP; tok += kCWarps) {
       float mx = 0.f;
       if (tok < A.M) {
         const uint4* row = reinterpret_cast<const uint4*>(xr + (int64_t)tok * KPW);
@@ -682,10 +681,9 @@ FP4X_DEV void w6_groups4(const WarpCtx& c, uint32_t a0, const uint32_t (&hb)[2],
 // 32 scale bytes per row), NCHK 4 the one-box stage (256 k: 64-byte high-bit rows, 16 scale bytes).  Every
 // address of the stage is a per-thread base XOR a constant: the bases have the varying bits clear (1024-aligned
 // planes, whole rows), and the varying parts (chunk pair, group) sit in bits the thread's fixed parts leave free.
-// The two-box stage runs as two four-group halves, which bounds the registers a warp holds; HALVES = 1 runs only
-// half `half0` of each box (four k-groups per stage).
-template <int NT, int NCHK, int HALVES = NCHK / 4>
-FP4X_DEV void stage_w6(const WarpCtx& c, int b, int c0, float (&acc)[NT][4], int half0 = 0) {
+// The two-box stage runs as two four-group halves, which bounds the registers a warp holds.
+template <int NT, int NCHK>
+FP4X_DEV void stage_w6(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) {
   constexpr int BI1 = NCHK == 8 ? 128 : 64;
   constexpr int SB = NCHK == 8 ? 32 : 16;
   const int G0 = b * 8 + c0;
@@ -700,8 +698,7 @@ FP4X_DEV void stage_w6(const WarpCtx& c, int b, int c0, float (&acc)[NT][4], int
   float accs[2][NT][4];
   zero_accs<NT, 2>(accs);
 #pragma unroll
-  for (int hh = 0; hh < HALVES; ++hh) {
-    const int half = half0 + hh;
+  for (int half = 0; half < NCHK / 4; ++half) {
     const uint32_t hbh[2] = {hb[0] ^ (32u * half), hb[1] ^ (32u * half)};
     const uint32_t sbh[2] = {sb[0] + 8u * half, sb[1] + 8u * half};
     w6_groups4<NT>(c, a0 ^ (64u * half), hbh, sbh, G0 + 4 * half, accs);
@@ -838,15 +835,9 @@ FP4X_DEV void stage_range(const WarpCtx& c, int b, int c0, float (&acc)[NT][4]) 
 // the fully unrolled stage bodies are large, and a kernel carrying all three shapes runs out of instruction cache.
 enum StageShape : int { SHAPE_128x2 = 0, SHAPE_128x1 = 1, SHAPE_64x1 = 2 };
 
-// KG = 4 (W8 and W6 two-box stages only): k-group kg takes half of box kg / 2 -- one W8 64-group, or four W6
-// 32-groups.
-template <int FMT, int NT, int SHAPE, int KG = kKG>
+template <int FMT, int NT, int SHAPE>
 FP4X_DEV void compute_stage(const WarpCtx& c, int kg, float (&acc)[NT][4]) {
-  if constexpr (KG == 4) {
-    static_assert(SHAPE == SHAPE_128x2 && (FMT == FMT_W8 || FMT == FMT_W6), "four k-groups: W8 / W6 two-box stages");
-    if constexpr (FMT == FMT_W8) stage_w8<NT, 4>(c, kg >> 1, 4 * (kg & 1), acc);
-    else stage_w6<NT, 8, 1>(c, kg >> 1, 0, acc, kg & 1);
-  } else if constexpr (SHAPE == SHAPE_128x2) {
+  if constexpr (SHAPE == SHAPE_128x2) {
     stage_range<FMT, NT, 8>(c, kg, 0, acc);
   } else if constexpr (SHAPE == SHAPE_128x1) {
     stage_range<FMT, NT, 4>(c, 0, 4 * kg, acc);
@@ -972,11 +963,8 @@ FP4X_DEV void run_epilogue(const GemvArgs& A, const GemvItem& it, int row0, cons
 // ------------------------------------------------------------------------------------------------------
 // the kernel
 // ------------------------------------------------------------------------------------------------------
-// KG k-groups of kRW row warps consume each stage (2, or 4 for W8 / W6 two-box stages of plans with one CTA per
-// SM: twice the warps to hide the decode latency of a CTA that has its SM to itself).
-template <int FMT, int NT, int EPI, int SHAPE, int KG = kKG>
+template <int FMT, int NT, int EPI, int SHAPE>
 FP4X_DEV void gemv_body(const GemvArgs& A) {
-  constexpr int CW = kRW * KG;  // consumer warps; warp CW is the producer
   extern __shared__ __align__(16) uint8_t smem_raw[];
   // stages need 1024-byte alignment for the swizzled TMA tiles; the host adds 1 KB of slack
   uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -1012,11 +1000,11 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
     FP4X_TL(tl_first(A.tl, kTlStartFirst); tl_last(A.tl, kTlStartLast));  // timeline: CTA start
     for (int s = 0; s < A.NS; ++s) {
       mbar_init(full0 + 8 * s, 33);
-      mbar_init(empty0 + 8 * s, CW);
+      mbar_init(empty0 + 8 * s, kCWarps);
     }
     mbar_init(xbar, 1);
     for (int i = 0; i < kRW; ++i) {
-      mbar_init(comb_full0 + 8 * i, KG - 1);
+      mbar_init(comb_full0 + 8 * i, 1);
       mbar_init(comb_empty0 + 8 * i, 1);
       if (A.cluster > 1) mbar_init(red_full0 + 8 * i, A.cluster - 1);
     }
@@ -1026,7 +1014,7 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
   // the leader's barriers must be initialised before another CTA of the cluster arrives on them
   if (A.cluster > 1) cluster_sync_all();
 
-  if (warp == CW) {
+  if (warp == kCWarps) {
     // ---------------- producer warp ----------------
     pdl_launch_dependents();
     const int tx = kRB * (A.NB0 * A.BI0 + (G.n1 ? A.BI1 : 0));
@@ -1079,8 +1067,8 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
   const int wrow = warp & (kRW - 1), kg = warp / kRW;
   pdl_wait();
   FP4X_TL(if (threadIdx.x == 0) { tl_last(A.tl, kTlWaitLast); tl_first(A.tl, kTlWaitFirst); });
-  stage_activations<FMT, NT, CW>(A, it, base, MP, k_panel0, xbar);
-  named_bar(1, CW * 32);
+  stage_activations<FMT, NT>(A, it, base, MP, k_panel0, xbar);
+  named_bar(1, kCWarps * 32);
   pdl_launch_dependents();
   FP4X_TL(if (threadIdx.x == 0) tl_last(A.tl, kTlStaged));
 
@@ -1104,35 +1092,29 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
   int cur = -1;
   bool ok = true;
   uint32_t nflush = 0;
-  // hand-over slots: [KG - 1][kRW][32 lanes][NT float4], slot kg - 1 written by k-group kg
   float* comb = reinterpret_cast<float*>(base + A.smem_comb) + (wrow * 32 + lane) * (NT * 4);
-  constexpr int kCombSlot = kRW * 32 * NT * 4;  // floats per slot
 
   auto flush = [&](int blk) {
-    // k-groups 1..KG-1 hand their partial sums for these 16 rows to k-group 0 through shared memory
+    // k-group 1 hands its partial sums for these 16 rows to k-group 0 through shared memory
     const uint32_t cf_bar = comb_full0 + 8 * wrow, ce_bar = comb_empty0 + 8 * wrow;
     const uint32_t par = nflush & 1u;
     ++nflush;
-    if (kg > 0) {
+    if (kg == 1) {
       // the previous block's sums must have been read before this block's overwrite them
       if (nflush > 1 && !mbar_wait_bounded(ce_bar, par ^ 1u, A.err)) { ok = false; return; }
-      float* mine = comb + (kg - 1) * kCombSlot;
 #pragma unroll
       for (int t = 0; t < NT; ++t)
-        *reinterpret_cast<float4*>(mine + 4 * t) = make_float4(acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
+        *reinterpret_cast<float4*>(comb + 4 * t) = make_float4(acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
       __syncwarp();
       if (lane == 0) mbar_arrive(cf_bar);
       return;
     }
     if (!mbar_wait_bounded(cf_bar, par, A.err)) { ok = false; return; }
-    // the k-groups in order 1, 2, ... (a fixed sum order)
 #pragma unroll
-    for (int j = 0; j < KG - 1; ++j)
-#pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        const float4 o = *reinterpret_cast<const float4*>(comb + j * kCombSlot + 4 * t);
-        acc[t][0] += o.x; acc[t][1] += o.y; acc[t][2] += o.z; acc[t][3] += o.w;
-      }
+    for (int t = 0; t < NT; ++t) {
+      const float4 o = *reinterpret_cast<const float4*>(comb + 4 * t);
+      acc[t][0] += o.x; acc[t][1] += o.y; acc[t][2] += o.z; acc[t][3] += o.w;
+    }
     __syncwarp();
     if (lane == 0) mbar_arrive(ce_bar);
     FP4X_TL(if (lane == 0) tl_last(A.tl, kTlHandover));
@@ -1282,7 +1264,7 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
     wc.p1 = stage + A.off_p1;
     wc.sc = stage + A.off_sc;
     wc.xb = xrow + chunk * steps_per_stage * 32;
-    compute_stage<FMT, NT, SHAPE, KG>(wc, kg, acc);
+    compute_stage<FMT, NT, SHAPE>(wc, kg, acc);
     __syncwarp();
     if (lane == 0) mbar_arrive(empty0 + 8 * s);
     if (++s == A.NS) { s = 0; phase ^= 1u; }
@@ -1303,12 +1285,6 @@ __global__ void __launch_bounds__(kThreads, 2) gemv_kernel(const __grid_constant
 template <int FMT, int NT, int EPI, int SHAPE>
 __global__ void __maxnreg__(128) gemv_kernel_wide(const __grid_constant__ GemvArgs A) {
   gemv_body<FMT, NT, EPI, SHAPE>(A);
-}
-// four k-groups (16 consumer warps + the producer, one CTA per SM: at most 120 registers a thread)
-constexpr int kThreadsKG4 = (kRW * 4 + 1) * 32;
-template <int FMT, int NT, int EPI, int SHAPE>
-__global__ void __launch_bounds__(kThreadsKG4, 1) gemv_kernel_kg4(const __grid_constant__ GemvArgs A) {
-  gemv_body<FMT, NT, EPI, SHAPE, 4>(A);
 }
 
 }  // namespace fp4x

@@ -13,7 +13,6 @@ struct Plan {
   int smem_x, smem_misc, smem_scr, smem_xraw, smem_comb, smem_red, smem_total;
   int xdirect;  // 16-token plans: the raw activation panel stays in global memory
   int cluster;
-  int KG;        // k-groups: 2, or 4 (gemv_kernel_kg4)
   size_t ws_bytes;
   int64_t counters;
 };
@@ -40,13 +39,6 @@ template <int FMT, int NT, int EPI, int SHAPE>
 int launch_s(const Plan& pl, const GemvArgs& a, int64_t batch, cudaStream_t st) {
   const bool wide = (int64_t)pl.CPP * pl.KP * batch <= device_facts().sms;
   auto kern = wide ? gemv_kernel_wide<FMT, NT, EPI, SHAPE> : gemv_kernel<FMT, NT, EPI, SHAPE>;
-  int threads = kThreads;
-  if constexpr (SHAPE == SHAPE_128x2 && (FMT == FMT_W8 || FMT == FMT_W6)) {
-    if (pl.KG == 4) {
-      kern = gemv_kernel_kg4<FMT, NT, EPI, SHAPE>;
-      threads = kThreadsKG4;
-    }
-  }
   cudaError_t e = ensure_smem_attr((const void*)kern, pl.smem_total);
   if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
   if (pl.cluster > 1) {
@@ -54,11 +46,11 @@ int launch_s(const Plan& pl, const GemvArgs& a, int64_t batch, cudaStream_t st) 
       e = ensure_nonportable_cluster((const void*)kern);
       if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute(non-portable cluster)");
     }
-    return check_launch(launch_pdl_cluster(kern, dim3(pl.CPP, pl.KP, (unsigned)batch), dim3(threads), pl.smem_total,
+    return check_launch(launch_pdl_cluster(kern, dim3(pl.CPP, pl.KP, (unsigned)batch), dim3(kThreads), pl.smem_total,
                                            st, pl.cluster, a),
                         "gemv cluster launch");
   }
-  return check_launch(launch_pdl(kern, dim3(pl.CPP, pl.KP, (unsigned)batch), dim3(threads), pl.smem_total, st, a),
+  return check_launch(launch_pdl(kern, dim3(pl.CPP, pl.KP, (unsigned)batch), dim3(kThreads), pl.smem_total, st, a),
                       "gemv launch");
 }
 
