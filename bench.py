@@ -287,34 +287,61 @@ class DecodeStep:
         return coarse, exact, gidx, None
 
     def capture(self):
-        """Capture the layers and the local head in one graph; returns the number of library kernels per step."""
+        """Capture the layers, the local head and (N > 1) the NCCL candidate exchange and the merge in one graph;
+        returns the number of library kernels per step.  If the exchange cannot be captured, the layers and the
+        local head are captured alone and the exchange runs eagerly after each replay (`self.exchange`)."""
         import fp4x_native as N
-        self.body()  # eager run: sizes the persistent counters, loads modules
+        local = self.body()  # eager run: sizes the persistent counters, loads modules
+        self.merged = None
+        self.exchange = "none (one GPU holds the whole vocabulary)" if self.world == 1 else "in graph"
+        if self.world > 1:
+            self._exchange(local)  # eager once: communicator set-up and lazy allocations before the capture
         torch.cuda.synchronize(self.dev)
-        s = torch.cuda.Stream(self.dev)
-        s.wait_stream(torch.cuda.current_stream(self.dev))
-        self.graph = torch.cuda.CUDAGraph()
-        n0 = N.launch_count()
-        with torch.cuda.stream(s):
-            with torch.cuda.graph(self.graph, stream=s):
-                self.local = self.body()
+        for attempt in range(2):
+            s = torch.cuda.Stream(self.dev)
+            s.wait_stream(torch.cuda.current_stream(self.dev))
+            self.graph = torch.cuda.CUDAGraph()
+            n0 = N.launch_count()
+            try:
+                with torch.cuda.stream(s):
+                    with torch.cuda.graph(self.graph, stream=s):
+                        self.local = self.body()
+                        if self.world > 1 and attempt == 0:
+                            self.merged = self._exchange(self.local)
+            except RuntimeError as e:
+                if attempt or self.world == 1:
+                    raise
+                self.graph, self.merged = None, None
+                self.exchange = "eager after the graph (capture failed: %s)" % str(e).splitlines()[0][:120]
+                torch.cuda.synchronize(self.dev)
+                continue
+            break
         torch.cuda.current_stream(self.dev).wait_stream(s)
         torch.cuda.synchronize(self.dev)
         return N.launch_count() - n0
 
+    def _exchange(self, local):
+        from fp4x_shard import gather_candidates
+        coarse, exact, gidx, _ = local
+        co, ex, gi = gather_candidates(coarse, exact, gidx)
+        return self.F.head_merge(co, ex, gi, VOCAB)
+
     def step(self):
-        """One decode step: graph replay, then (N > 1) the candidate exchange and merge; returns (idx, argmax)."""
+        """One decode step: graph replay (with N > 1 the candidate exchange and merge are in the graph, unless their
+        capture failed); returns (idx, argmax)."""
         self.graph.replay()
         coarse, exact, gidx, amax = self.local
         if self.world == 1:
             return gidx, amax
-        from fp4x_shard import gather_candidates
-        co, ex, gi = gather_candidates(coarse, exact, gidx)
-        idx, _, _, amax = self.F.head_merge(co, ex, gi, VOCAB)
+        if self.merged is not None:
+            idx, _, _, amax = self.merged
+            return idx, amax
+        idx, _, _, amax = self._exchange(self.local)
         return idx, amax
 
     def merge_launches(self):
-        return 0 if self.world == 1 else 1
+        """Library kernels per step outside the graph (the merge, when the exchange runs eagerly)."""
+        return 1 if (self.world > 1 and self.merged is None) else 0
 
     def exchange_timings(self, reps=20):
         """Device times (µs) of the pieces of the sharded head: the local head alone, the NCCL all-gather of the
@@ -329,19 +356,36 @@ class DecodeStep:
         for _ in range(3):
             co, ex, gi = gather_candidates(coarse, exact, gidx)
         torch.cuda.synchronize(self.dev)
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(st)
-        for _ in range(reps):
-            co, ex, gi = gather_candidates(coarse, exact, gidx)
-        e1.record(st)
-        torch.cuda.synchronize(self.dev)
-        out["allgather_us"] = round(e0.elapsed_time(e1) * 1e3 / reps, 2)
-        e0.record(st)
-        for _ in range(reps):
-            self.F.head_merge(co, ex, gi, VOCAB)
-        e1.record(st)
-        torch.cuda.synchronize(self.dev)
-        out["merge_us"] = round(e0.elapsed_time(e1) * 1e3 / reps, 2)
+
+        def timed(fn):
+            # as the step runs them: replayed from a graph when the exchange is captured, eagerly otherwise
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            if self.merged is None:
+                e0.record(st)
+                for _ in range(reps):
+                    fn()
+                e1.record(st)
+                torch.cuda.synchronize(self.dev)
+                return round(e0.elapsed_time(e1) * 1e3 / reps, 2)
+            s = torch.cuda.Stream(self.dev)
+            s.wait_stream(st)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.stream(s):
+                with torch.cuda.graph(g, stream=s):
+                    for _ in range(reps):
+                        fn()
+            st.wait_stream(s)
+            g.replay()
+            torch.cuda.synchronize(self.dev)
+            e0.record(st)
+            g.replay()
+            e1.record(st)
+            torch.cuda.synchronize(self.dev)
+            del g  # holds NCCL work: released before the process group goes
+            return round(e0.elapsed_time(e1) * 1e3 / reps, 2)
+
+        out["allgather_us"] = timed(lambda: gather_candidates(coarse, exact, gidx))
+        out["merge_us"] = timed(lambda: self.F.head_merge(co, ex, gi, VOCAB))
         return out
 
 
@@ -858,6 +902,7 @@ def native_arm(args):
             "class_us": {k: round(v, 2) for k, v in per_class.items()} | {"fast_head": round(head_us, 2)},
             "step_kernel_us": None if step_us is None else round(step_us, 2),
             "sharded_head_us": exchange,
+            "candidate_exchange": step.exchange,
             "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": "GB/s", "ms_per_step": round(ms_e2e, 4),
                     "h2d_bytes_per_step": h_host.numel() * 2 + s_host.numel() * 2,
