@@ -857,7 +857,8 @@ FP4X_DEV void hc_down_store(__nv_bfloat16* di, __nv_bfloat16* bot, int N, int lr
   const __nv_bfloat16 d = __float2bfloat16_rn(v);
   di[(int64_t)m * N + n] = d;
   if (n < lr && bot) {
-    const float t = bf16_round(__bfloat162float(d) / (float)hc);
+    const float f = __bfloat162float(d);
+    const float t = bf16_round(hc == 4 ? f * 0.25f : f / (float)hc);  // / 4 is exact as * 0.25
     bot[(int64_t)m * lr + n] = __float2bfloat16_rn(t * sigmoidf_(t));
   }
 }
@@ -943,6 +944,22 @@ FP4X_DEV void run_epilogue(const GemvArgs& A, const GemvItem& it, int row0, cons
       const int H = A.N / A.hc;
       const __nv_bfloat16* nrm = reinterpret_cast<const __nv_bfloat16*>(A.nrm);
       const int nout = A.bj * A.M;
+      if (A.hc == 4) {
+        // four streams (the served and benchmarked geometry): the loads of an output issue together and the
+        // values stay in registers; the same products and the same pairwise sum order as hc_gate_mean, and
+        // the division by 4 is exact as a multiplication
+        for (int o = lane + 32 * (warp - first_warp); o < nout; o += 32 * nwarps) {
+          const int m = o / A.bj, cidx = o - m * A.bj;
+          const int col = jb * A.bj + cidx;
+          const __nv_bfloat16* nr = nrm + (int64_t)m * A.nrm_stride + col;
+          float p[4];
+#pragma unroll
+          for (int s4 = 0; s4 < 4; ++s4)
+            p[s4] = bf16_round(__bfloat162float(nr[s4 * H]) * bscr[(s4 * A.bj + cidx) * MP + m]);
+          reinterpret_cast<__nv_bfloat16*>(it.out)[(int64_t)m * A.out_stride + col] =
+              __float2bfloat16_rn(bf16_round(((p[0] + p[1]) + (p[2] + p[3])) * 0.25f));
+        }
+      } else
       for (int o = lane + 32 * (warp - first_warp); o < nout; o += 32 * nwarps) {
         const int m = o / A.bj, cidx = o - m * A.bj;
         const int col = jb * A.bj + cidx;
