@@ -26,15 +26,17 @@ static int launch_nv4_tc(const tc::Args& a, unsigned grid, int smem_total, void*
       "nv4 tcgen05 launch");
 }
 
-// NVFP4 on tcgen05 block-scaled MMAs (fp4x_tc.cuh): M <= 8 tokens, at least 64 row blocks of 128, K a multiple
-// of 256.  Returns 1 when the shape is not covered (the caller then uses the register-decode kernel).
+// NVFP4 on tcgen05 block-scaled MMAs (fp4x_tc.cuh): M <= 16 tokens (9-16 run the 12- or 16-token kernel), at least
+// 64 row blocks of 128, K a multiple of 256.  Returns 1 when the shape is not covered (the caller then uses the
+// register-decode kernel).
 int run_nv4_tc(const void* x, int64_t x_stride, const void* wp, const void* sc, float gs, void* out,
                       int64_t out_stride, int out_dtype, int64_t m, int64_t n, int64_t k, void* stream) {
   const DeviceFacts& dv = device_facts();
   if (m < 1 || m > tc::kMaxM || k % tc::kKC != 0 || k / tc::kKC > tc::kMaxSlabs || n < 64 * tc::kRows ||
       n > (1 << 30))
     return 1;
-  const int NB = (tc::kTerms * (int)m + 15) / 16 * 16;
+  const int mt = m <= 8 ? (int)m : (m <= 12 ? 12 : 16);  // the kernel's token count
+  const int NB = (tc::kTerms * mt + 15) / 16 * 16;
   if (4 * (k / 64) > tc::kTmemCols - tc::kColSFB || NB > tc::kColSFA) return 1;
   if (!aligned(x, 16) || x_stride % 8 != 0 || x_stride < k || !aligned(wp, 16) || (k / 2) % 16 != 0) return 1;
   const int64_t lds = k / 16;
@@ -44,7 +46,7 @@ int run_nv4_tc(const void* x, int64_t x_stride, const void* wp, const void* sc, 
   tc::Args a;
   std::memset(&a, 0, sizeof(a));
   const int b_bytes = (int)(k / 256) * NB * 128;
-  const int xraw = round_up((int)(m * k * 2), 1024);
+  const int xraw = mt > 8 ? 0 : round_up((int)(m * k * 2), 1024);  // more than 8 tokens are read through L2
   const int sfb = round_up((int)(k / 64) * 512, 1024);  // B scales in tcgen05.cp groups, one per 64-k block
   const int fixed = b_bytes + xraw + sfb + tc::kMiscBytes + 1024;
   int ns = (dv.smem_optin - fixed) / tc::kStageBytes;
@@ -74,7 +76,9 @@ int run_nv4_tc(const void* x, int64_t x_stride, const void* wp, const void* sc, 
     case 5: return launch_nv4_tc<5>(a, grid, smem_total, stream);
     case 6: return launch_nv4_tc<6>(a, grid, smem_total, stream);
     case 7: return launch_nv4_tc<7>(a, grid, smem_total, stream);
-    default: return launch_nv4_tc<8>(a, grid, smem_total, stream);
+    case 8: return launch_nv4_tc<8>(a, grid, smem_total, stream);
+    default: return mt == 12 ? launch_nv4_tc<12>(a, grid, smem_total, stream)
+                             : launch_nv4_tc<16>(a, grid, smem_total, stream);
   }
 }
 
@@ -92,7 +96,7 @@ static int launch_mx8_tc(const tc::MxArgs& a, unsigned grid, int smem_total, voi
 int run_mx8_tc(const void* x, int64_t x_stride, const void* w, const void* sc, void* out, int64_t out_stride,
                       int out_dtype, int64_t m, int64_t n, int64_t k, void* stream) {
   const DeviceFacts& dv = device_facts();
-  if (m < 1 || m > tc::kMaxM || k % 512 != 0 || k / tc::kMxKC > tc::kMxMaxChunks || n < 64 * tc::kRows ||
+  if (m < 1 || m > tc::kMxMaxM || k % 512 != 0 || k / tc::kMxKC > tc::kMxMaxChunks || n < 64 * tc::kRows ||
       n > (1 << 30))
     return 1;
   if (!aligned(x, 16) || x_stride % 8 != 0 || x_stride < k || !aligned(w, 16) || !aligned(sc, 16) || !out ||

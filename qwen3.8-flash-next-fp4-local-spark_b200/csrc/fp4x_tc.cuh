@@ -16,7 +16,7 @@
 // range; after T = 6 terms the remainder is below 2^-13 of the token's largest element (the products themselves are
 // exact and accumulate in fp32).  The epilogue recombines the term columns with the factors 2^(e0 - 2t).
 //
-// Roles (384 threads; 576 at 5-8 tokens): warp 0 streams weight tiles and their scale tiles (TMA); warp 1 owns the
+// Roles (384 threads; 576 at 5-8 tokens, 704 at 9-16): warp 0 streams weight tiles and their scale tiles (TMA); warp 1 owns the
 // tensor memory and one of its lanes issues the MMAs; warps 2..7 (and 12..17 at 5-8 tokens) turn the activations into
 // e2m1 terms after the grid-dependency wait, slab by slab (256 k), so the MMAs of the first slabs start while later
 // slabs are still being prepared; warps 8..11 (tensor-memory subpartitions 0..3) write each stage's A scales and
@@ -34,14 +34,16 @@ constexpr int kThreads = 384;
 // NVFP4 at 5-8 tokens: six more term-preparation warps (12..17), so each SM sub-partition runs three of them.  On a
 // 16384 x 2560 GEMV this took 5 / 6 / 7 / 8 tokens from 11.2 / 12.4 / 14.0 / 14.9 us to 10.7 / 11.4 / 12.1 / 12.8 us;
 // at 1-4 tokens it made no difference or was slower.
-__host__ __device__ constexpr int nv_prep_extra(int mt) { return mt >= 5 ? 6 : 0; }
+// At 12 / 16 tokens (activations read through L2, 77 registers a thread): ten more, 704 threads in all.
+__host__ __device__ constexpr int nv_prep_extra(int mt) { return mt > 8 ? 10 : (mt >= 5 ? 6 : 0); }
 __host__ __device__ constexpr int nv_threads(int mt) { return kThreads + 32 * nv_prep_extra(mt); }
 constexpr int kRows = 128;          // MMA M
 constexpr int kKC = 256;            // k per stage (128 bytes of e2m1 per row)
 constexpr int kMaxStages = 8;
 constexpr int kMaxSlabs = 16;       // 256-k activation slabs: K <= 4096
 constexpr int kTerms = 6;
-constexpr int kMaxM = 8;            // tokens: kTerms * 8 = 48 B columns
+constexpr int kMaxM = 16;           // NVFP4 tokens: kTerms * 16 = 96 B columns
+constexpr int kMxMaxM = 8;          // MXFP8 tokens
 constexpr int kTmemCols = 512;
 // tensor-memory column plan: accumulators, A scales (16 columns per stage), B scales (4 columns per 64-k block: the
 // B-scale tile is laid out for 128 columns of B whatever the MMA's N, so each k-block's slot starts 4-aligned).
@@ -208,10 +210,15 @@ FP4X_DEV uint32_t b_offset(int NB, int n, int k) {
   return (uint32_t)(slab * NB * 128 + (n >> 3) * 1024 + r * 128 + ((chunk ^ r) << 4) + (byte & 15));
 }
 
+// MT = 1..8 is the exact token count.  MT = 12 and 16 serve 9-12 and 13-16 tokens (A.M <= MT; the B columns of the
+// missing tokens are not prepared and their outputs not stored): their activations are read through L2 instead of
+// being copied into shared memory (the 96 B columns of 16 tokens take 120 KB there), and the epilogue folds the
+// term columns chunk by chunk.
 template <int MT>
 __global__ void __launch_bounds__(nv_threads(MT), 1) nv4_tc_kernel(const __grid_constant__ Args A) {
   constexpr int NBT = (kTerms * MT + 15) / 16 * 16;
-  constexpr int NACC = NBT <= 32 ? 4 : 2;  // accumulators of NBT columns within the 128 columns at kColD
+  constexpr int NACC = NBT <= 32 ? 4 : (NBT <= 64 ? 2 : 1);  // accumulators of NBT columns in the 128 at kColD
+  constexpr bool kXGlobal = MT > 8;
   constexpr int kBlkPerSlab = MT * 16;     // 16-element activation blocks per 256-k slab (all tokens)
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -333,7 +340,40 @@ __global__ void __launch_bounds__(nv_threads(MT), 1) nv4_tc_kernel(const __grid_
     if (ok && !mbar_wait_bounded(dfull, 0, A.err)) ok = false;
     FP4X_TL(if (sub == 0 && lane == 0) tl_last(A.tl, kTlLoopDone));
     tc_fence_after();
-    if (ok) {
+    if (ok && kXGlobal) {
+      // one accumulator; columns read from the last chunk down, so every token's terms are added smallest first
+      // (t = kTerms - 1 .. 0), as below
+      float accm[MT];
+#pragma unroll
+      for (int m = 0; m < MT; ++m) accm[m] = 0.f;
+#pragma unroll
+      for (int c0 = NBT - 16; c0 >= 0; c0 -= 16) {
+        uint32_t q[16];
+        tc_ld16(tsub + kColD + (uint32_t)c0, q);
+        tc_wait_ld();
+#pragma unroll
+        for (int i = 15; i >= 0; --i) {
+          const int col = c0 + i;
+          if (col < kTerms * MT) {
+            const int t = col / MT, m = col - t * MT;
+            accm[m] = fmaf(__uint_as_float(q[i]), __uint_as_float((uint32_t)(127 - 2 * t) << 23), accm[m]);
+          }
+        }
+      }
+      const int row = row0 + 32 * sub + lane;
+      if (row < A.N) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          if (m < A.M) {
+            const uint32_t mb = amax_bits[m];
+            const int e0 = max(min(mb ? (int)(mb >> 23) - 127 : 0, 126), -126);
+            store_out(A.out, A.out_dtype, (int64_t)m * A.out_stride + row,
+                      accm[m] * __uint_as_float((uint32_t)(e0 + 127) << 23) * A.gs);
+          }
+        }
+      }
+      FP4X_TL(if (lane == 0) tl_last(A.tl, kTlStored));
+    } else if (ok) {
       float d[NBT];
 #pragma unroll
       for (int i = 0; i < NBT; ++i) d[i] = 0.f;
@@ -371,31 +411,51 @@ __global__ void __launch_bounds__(nv_threads(MT), 1) nv4_tc_kernel(const __grid_
     const int ptid = warp < 8 ? threadIdx.x - 64 : threadIdx.x - 192, pthreads = 192 + 32 * nv_prep_extra(MT);
     pdl_wait();
     FP4X_TL(if (ptid == 0) { tl_last(A.tl, kTlWaitLast); tl_first(A.tl, kTlWaitFirst); });
+    // token m's row: the raw panel in shared memory (MT <= 8) or the activations themselves through L2
     const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(base + A.smem_xraw);
-    if (ptid == 0) {
-      const uint32_t bytes = (uint32_t)A.K * 2u;
-      mbar_arrive_expect_tx(xbar, bytes * (uint32_t)MT);
-      for (int m = 0; m < MT; ++m)
-        bulk_g2s(smem_u32(base + A.smem_xraw) + m * bytes, A.x + (int64_t)m * A.x_stride, bytes, xbar);
+    auto xrow = [&](int m) -> const __nv_bfloat16* {
+      return kXGlobal ? A.x + (int64_t)m * A.x_stride : xr + (int64_t)m * A.K;
+    };
+    if constexpr (!kXGlobal) {
+      if (ptid == 0) {
+        const uint32_t bytes = (uint32_t)A.K * 2u;
+        mbar_arrive_expect_tx(xbar, bytes * (uint32_t)MT);
+        for (int m = 0; m < MT; ++m)
+          bulk_g2s(smem_u32(base + A.smem_xraw) + m * bytes, A.x + (int64_t)m * A.x_stride, bytes, xbar);
+      }
+      if (!mbar_wait_bounded(xbar, 0, A.err)) ok = false;
     }
-    if (!mbar_wait_bounded(xbar, 0, A.err)) ok = false;
     FP4X_TL(if (ptid == 0) tl_last(A.tl, kTlXLanded));
-    if (ok) {
-      for (int m = 0; m < MT; ++m) {
-        uint32_t mx = 0;
-        for (int i = ptid; i < A.K / 8; i += pthreads) {
-          const uint4 q = reinterpret_cast<const uint4*>(xr + (int64_t)m * A.K)[i];
-          const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+    {
+      // every token's maximum in one pass: the loads of all tokens are in flight together (through L2 at MT > 8),
+      // then one interleaved warp reduction
+      uint32_t mx[MT];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            mx = max(mx, (w4[e] << 17) >> 1);  // |lo| as fp32 bits
-            mx = max(mx, (w4[e] >> 16 & 0x7fffu) << 16);
+      for (int m = 0; m < MT; ++m) mx[m] = 0u;
+      if (ok) {
+        for (int i = ptid; i < A.K / 8; i += pthreads) {
+#pragma unroll
+          for (int m = 0; m < MT; ++m) {
+            if (!kXGlobal || m < A.M) {
+              const uint4 q = kXGlobal ? __ldcg(reinterpret_cast<const uint4*>(xrow(m)) + i)
+                                       : reinterpret_cast<const uint4*>(xrow(m))[i];
+              const uint32_t w4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                mx[m] = max(mx[m], (w4[e] << 17) >> 1);  // |lo| as fp32 bits
+                mx[m] = max(mx[m], (w4[e] >> 16 & 0x7fffu) << 16);
+              }
+            }
           }
         }
-#pragma unroll
-        for (int o = 16; o; o >>= 1) mx = max(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-        if (lane == 0) atomicMax(amax_bits + m, mx);
       }
+#pragma unroll
+      for (int o = 16; o; o >>= 1)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) mx[m] = max(mx[m], __shfl_xor_sync(0xffffffffu, mx[m], o));
+      if (lane == 0 && ok)
+#pragma unroll
+        for (int m = 0; m < MT; ++m) atomicMax(amax_bits + m, mx[m]);
     }
     named_bar(1, pthreads);
     FP4X_TL(if (ptid == 0) tl_last(A.tl, kTlStaged));
@@ -405,14 +465,17 @@ __global__ void __launch_bounds__(nv_threads(MT), 1) nv4_tc_kernel(const __grid_
     for (int idx = ptid; idx < nstages * kBlkPerSlab; idx += pthreads) {
       const int slab = idx / kBlkPerSlab, rem = idx - slab * kBlkPerSlab;
       const int m = rem >> 4, j = slab * 16 + (rem & 15);
-      if (ok) {
+      // tokens beyond A.M (MT > 8): their B columns reach only output columns that are not stored, so their terms
+      // and scales are left as they are
+      if (ok && (!kXGlobal || m < A.M)) {
         const uint32_t mb = amax_bits[m];
         // 2^-e0 with e0 the exponent of the token maximum (1 for an all-zero token)
         const int e0 = mb ? (int)(mb >> 23) - 127 : 0;
         const float pre = __uint_as_float((uint32_t)(127 - max(min(e0, 126), -126)) << 23);
         float v[16];
-        const uint4 q0 = reinterpret_cast<const uint4*>(xr + (int64_t)m * A.K + 16 * j)[0];
-        const uint4 q1 = reinterpret_cast<const uint4*>(xr + (int64_t)m * A.K + 16 * j)[1];
+        const uint4* src = reinterpret_cast<const uint4*>(xrow(m) + 16 * j);
+        const uint4 q0 = kXGlobal ? __ldcg(src) : src[0];
+        const uint4 q1 = kXGlobal ? __ldcg(src + 1) : src[1];
         const uint32_t w8[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
         for (int i = 0; i < 8; ++i) {

@@ -1,5 +1,6 @@
-"""GPU parity of the tcgen05 NVFP4 and MXFP8 GEMVs (shapes with M <= 8 tokens and at least 8,192 rows take the block-scaled
-tensor-core kernel; the others take the register-decode kernel, covered in test_gpu_gemv.py).
+"""GPU parity of the tcgen05 NVFP4 and MXFP8 GEMVs (shapes with at least 8,192 rows and M <= 16 tokens for NVFP4, M <= 8
+for MXFP8, take the block-scaled tensor-core kernel; the others take the register-decode kernel, covered in
+test_gpu_gemv.py).
 
 The tensor-core kernel multiplies the stored e2m1 weights and e4m3 scales exactly and writes each activation as six
 e2m1 terms with e4m3 block scales; what the terms leave out is below 9e-5 of the token's largest element.
@@ -52,6 +53,27 @@ def test_nv4_tc_clustered_terms_match_oracle(nv4_weights_16384, m):
     y32 = F.nv4_linear(xd, Pd, Sd, gs, out_dtype=torch.float32).cpu()
     assert rel_err(y32, ref) < 2e-4
     assert torch.equal(F.nv4_linear(xd, Pd, Sd, gs, out_dtype=torch.float32).cpu(), y32)
+
+
+@pytest.mark.parametrize("m", [9, 11, 12, 13, 16])
+def test_nv4_tc_16_tokens_matches_oracle(nv4_weights, nv4_weights_16384, m):
+    """9..16 tokens (C2(c) at M = 16) on the 12- and 16-token kernels: activations read through L2, the tokens
+    beyond M are zero blocks, the epilogue folds the term columns chunk by chunk."""
+    for P, S, gs, wdeq in (nv4_weights, nv4_weights_16384):
+        g = torch.Generator().manual_seed(500 + m)
+        x = torch.randn(m, K, generator=g).to(torch.bfloat16)
+        x[m // 2] *= 300.0  # one token far larger than the others: each token keeps its own pre-scale
+        ref = (x.double().numpy() @ wdeq.T) * np.float64(np.float32(gs))
+        Pd, Sd, xd = P.to(DEV), S.to(DEV), x.to(DEV)
+        y32 = F.nv4_linear(xd, Pd, Sd, gs, out_dtype=torch.float32).cpu()
+        for i in range(m):  # per token: the bound is relative to the token's own largest output
+            assert rel_err(y32[i], ref[i]) < 2e-4, i
+        yb = F.nv4_linear(xd, Pd, Sd, gs).cpu()
+        assert rel_err(yb.float(), ref) < 1e-2
+        # a strided activation view (rows of a wider buffer) gives the same bits
+        xw = torch.zeros(m, K + 64, dtype=torch.bfloat16, device=DEV)
+        xw[:, :K] = xd
+        assert torch.equal(F.nv4_linear(xw[:, :K], Pd, Sd, gs, out_dtype=torch.float32).cpu(), y32)
 
 
 @pytest.mark.parametrize("m", range(1, 9))
