@@ -121,19 +121,13 @@ FP4X_DEV uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(addr), "r"(rank));
   return r;
 }
-FP4X_DEV void st_cluster_v4(uint32_t addr, float a, float b, float c, float d) {
-  asm volatile("st.shared::cluster.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "f"(a), "f"(b), "f"(c), "f"(d)
+// asynchronous 16-byte store into another CTA of the cluster that completes its bytes on that CTA's mbarrier
+// (complete_tx): the receiver's wait on the barrier makes the data visible, no release fence or arrival is needed
+FP4X_DEV void st_async_v4(uint32_t cluster_addr, float a, float b, float c, float d, uint32_t cluster_bar) {
+  asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(
+                   cluster_addr),
+               "f"(a), "f"(b), "f"(c), "f"(d), "r"(cluster_bar)
                : "memory");
-}
-FP4X_DEV void st_cluster_v2(uint32_t addr, uint32_t a, uint32_t b) {
-  asm volatile("st.shared::cluster.v2.u32 [%0], {%1, %2};" ::"r"(addr), "r"(a), "r"(b) : "memory");
-}
-FP4X_DEV void st_cluster_u8(uint32_t addr, uint32_t v) {
-  asm volatile("st.shared::cluster.u8 [%0], %1;" ::"r"(addr), "r"(v) : "memory");
-}
-// arrive on an mbarrier of another CTA of the cluster, releasing this thread's prior writes at cluster scope
-FP4X_DEV void mbar_arrive_remote(uint32_t cluster_addr) {
-  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 FP4X_DEV bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
   uint32_t ok;

@@ -1023,7 +1023,13 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
     for (int i = 0; i < kRW; ++i) {
       mbar_init(comb_full0 + 8 * i, 1);
       mbar_init(comb_empty0 + 8 * i, 1);
-      if (A.cluster > 1) mbar_init(red_full0 + 8 * i, A.cluster - 1);
+      if (A.cluster > 1) {
+        // the leader arrives here once, expecting the other panels' partial sums as bytes (st.async complete_tx),
+        // before the cluster barrier below lets any of them store
+        mbar_init(red_full0 + 8 * i, 1);
+        if (cluster_ctarank() == 0)
+          mbar_arrive_expect_tx(red_full0 + 8 * i, (uint32_t)(A.cluster - 1) * 32u * NT * 16u);
+      }
     }
     mbar_init_fence();
   }
@@ -1143,9 +1149,9 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
     }
     const int row0 = blk * kRB + 16 * wrow;
     if (A.cluster > 1) {
-      // One row block per CTA; the CTAs of the block's K panels form the cluster.  Each non-leader writes its
-      // partial sums into the leader's shared memory and arrives on the leader's barrier for this row warp; the
-      // leader adds them in panel order and runs the epilogue.
+      // One row block per CTA; the CTAs of the block's K panels form the cluster.  Each non-leader stores its
+      // partial sums into the leader's shared memory with st.async, whose bytes complete the leader's barrier for
+      // this row warp; the leader adds them in panel order and runs the epilogue.
       const uint32_t rank = cluster_ctarank();
       constexpr uint32_t kSlot = 32u * NT * 16u;  // one row warp: 32 lanes x NT float4
       const uint32_t red = smem_u32(base + A.smem_red) + (uint32_t)wrow * kSlot + (uint32_t)lane * NT * 16u;
@@ -1158,10 +1164,11 @@ FP4X_DEV void gemv_body(const GemvArgs& A) {
           return;
         }
         const uint32_t dst = mapa_shared(red + (rank - 1) * kRW * kSlot, 0);
+        // asynchronous remote stores that complete their bytes on the leader's barrier: no release fence and no
+        // arrival (measured against st.shared::cluster + a release arrive: 0.1-0.4 µs less per launch)
+        const uint32_t rbar = mapa_shared(red_full0 + 8 * wrow, 0);
 #pragma unroll
-        for (int t = 0; t < NT; ++t) st_cluster_v4(dst + 16u * t, acc[t][0], acc[t][1], acc[t][2], acc[t][3]);
-        __syncwarp();
-        if (lane == 0) mbar_arrive_remote(mapa_shared(red_full0 + 8 * wrow, 0));
+        for (int t = 0; t < NT; ++t) st_async_v4(dst + 16u * t, acc[t][0], acc[t][1], acc[t][2], acc[t][3], rbar);
         return;
       }
       if (!mbar_wait_bounded_cluster(red_full0 + 8 * wrow, 0, A.err)) { ok = false; return; }
