@@ -87,12 +87,14 @@ static int launch_mx8_tc(const tc::MxArgs& a, unsigned grid, int smem_total, voi
   auto kern = tc::mx8_tc_kernel<MT>;
   cudaError_t e = ensure_smem_attr((const void*)kern, smem_total);
   if (e != cudaSuccess) return check_launch(e, "cudaFuncSetAttribute");
-  return check_launch(launch_pdl(kern, dim3(grid), dim3(tc::kThreads), (size_t)smem_total, (cudaStream_t)stream, a),
-                      "mx8 tcgen05 launch");
+  return check_launch(
+      launch_pdl(kern, dim3(grid), dim3(tc::mx_threads(MT)), (size_t)smem_total, (cudaStream_t)stream, a),
+      "mx8 tcgen05 launch");
 }
 
-// MXFP8 on tcgen05 block-scaled MMAs (fp4x_tc.cuh): M <= 8 tokens, at least 64 row blocks of 128, K a multiple of
-// 512 up to 4096.  Returns 1 when the shape is not covered (the caller then uses the register-decode kernel).
+// MXFP8 on tcgen05 block-scaled MMAs (fp4x_tc.cuh): M <= 16 tokens (9-16 run the 12- or 16-token kernel), at least
+// 64 row blocks of 128, K a multiple of 512 up to 4096.  Returns 1 when the shape is not covered (the caller then uses
+// the register-decode kernel).
 int run_mx8_tc(const void* x, int64_t x_stride, const void* w, const void* sc, void* out, int64_t out_stride,
                       int out_dtype, int64_t m, int64_t n, int64_t k, void* stream) {
   const DeviceFacts& dv = device_facts();
@@ -104,11 +106,12 @@ int run_mx8_tc(const void* x, int64_t x_stride, const void* w, const void* sc, v
     return 1;
   int rc;
   if ((rc = check_out_dtype(out_dtype))) return rc;
-  const int NB = (tc::kMxTerms * (int)m + 15) / 16 * 16;
+  const int mt = m <= 8 ? (int)m : (m <= 12 ? 12 : 16);  // the kernel's token count
+  const int NB = (tc::kMxTerms * mt + 15) / 16 * 16;
   tc::MxArgs a;
   std::memset(&a, 0, sizeof(a));
   const int b_bytes = (int)(k / tc::kMxKC) * NB * 128;
-  const int xraw = round_up((int)(m * k * 2), 1024);
+  const int xraw = mt > 8 ? 0 : round_up((int)(m * k * 2), 1024);  // more than 8 tokens are read through L2
   const int sfb = round_up((int)(k / tc::kMxKC) * 512, 1024);
   const int sfa = round_up(tc::kRows * (int)(k / 32), 1024);
   const int misc = 1024;
@@ -140,7 +143,9 @@ int run_mx8_tc(const void* x, int64_t x_stride, const void* w, const void* sc, v
     case 5: return launch_mx8_tc<5>(a, grid, smem_total, stream);
     case 6: return launch_mx8_tc<6>(a, grid, smem_total, stream);
     case 7: return launch_mx8_tc<7>(a, grid, smem_total, stream);
-    default: return launch_mx8_tc<8>(a, grid, smem_total, stream);
+    case 8: return launch_mx8_tc<8>(a, grid, smem_total, stream);
+    default: return mt == 12 ? launch_mx8_tc<12>(a, grid, smem_total, stream)
+                             : launch_mx8_tc<16>(a, grid, smem_total, stream);
   }
 }
 

@@ -43,7 +43,7 @@ constexpr int kMaxStages = 8;
 constexpr int kMaxSlabs = 16;       // 256-k activation slabs: K <= 4096
 constexpr int kTerms = 6;
 constexpr int kMaxM = 16;           // NVFP4 tokens: kTerms * 16 = 96 B columns
-constexpr int kMxMaxM = 8;          // MXFP8 tokens
+constexpr int kMxMaxM = 16;         // MXFP8 tokens
 constexpr int kTmemCols = 512;
 // tensor-memory column plan: accumulators, A scales (16 columns per stage), B scales (4 columns per 64-k block: the
 // B-scale tile is laid out for 128 columns of B whatever the MMA's N, so each k-block's slot starts 4-aligned).
@@ -560,10 +560,17 @@ FP4X_DEV uint32_t b_offset_mx(int NB, int n, int k) {
   return (uint32_t)(slab * NB * 128 + (n >> 3) * 1024 + r * 128 + ((chunk ^ r) << 4) + (byte & 15));
 }
 
+// As for NVFP4: MT = 1..8 is the exact token count, MT = 12 / 16 serve 9-16 tokens with the activations read
+// through L2 (the 64 B columns of 16 tokens take 160 KB of shared memory), the absent tokens' B columns left
+// unprepared, ten more preparation warps, and an epilogue that folds the columns chunk by chunk.
+__host__ __device__ constexpr int mx_prep_extra(int mt) { return mt > 8 ? 10 : 0; }
+__host__ __device__ constexpr int mx_threads(int mt) { return kThreads + 32 * mx_prep_extra(mt); }
+
 template <int MT>
-__global__ void __launch_bounds__(kThreads, 1) mx8_tc_kernel(const __grid_constant__ MxArgs A) {
+__global__ void __launch_bounds__(mx_threads(MT), 1) mx8_tc_kernel(const __grid_constant__ MxArgs A) {
   constexpr int NBT = (kMxTerms * MT + 15) / 16 * 16;
   constexpr int NACC = NBT <= 32 ? 4 : 2;
+  constexpr bool kXGlobal = MT > 8;
   constexpr int kBlkPerSlab = MT * 4;  // 32-element activation blocks per 128-k slab (all tokens)
   extern __shared__ __align__(16) uint8_t smem_raw[];
   uint8_t* base = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
@@ -645,7 +652,7 @@ __global__ void __launch_bounds__(kThreads, 1) mx8_tc_kernel(const __grid_consta
       tc_commit(dfull);
     }
     __syncwarp();
-  } else if (warp >= 8) {
+  } else if (warp >= 8 && warp < 12) {
     // ---------------- scale writers (subpartition warp - 8), then the epilogue ----------------
     const int sub = warp - 8;
     const uint32_t tsub = tmem + ((uint32_t)(32 * sub) << 16);
@@ -679,7 +686,42 @@ __global__ void __launch_bounds__(kThreads, 1) mx8_tc_kernel(const __grid_consta
     }
     if (ok && !mbar_wait_bounded(dfull, 0, A.err)) ok = false;
     tc_fence_after();
-    if (ok) {
+    if (ok && kXGlobal) {
+      // columns from the last chunk down: every token's terms are added t = kMxTerms - 1 .. 0, each column being
+      // the accumulators summed in order, as below
+      float accm[MT];
+#pragma unroll
+      for (int m = 0; m < MT; ++m) accm[m] = 0.f;
+#pragma unroll
+      for (int c0 = NBT - 16; c0 >= 0; c0 -= 16) {
+        float dc[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) dc[i] = 0.f;
+#pragma unroll
+        for (int a = 0; a < NACC; ++a) {
+          uint32_t q[16];
+          tc_ld16(tsub + kMxColD + (uint32_t)(a * NBT + c0), q);
+          tc_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) dc[i] += __uint_as_float(q[i]);
+        }
+#pragma unroll
+        for (int i = 15; i >= 0; --i) {
+          const int col = c0 + i;
+          if (col < kMxTerms * MT) {
+            const int t = col / MT, m = col - t * MT;
+            accm[m] += dc[i];
+            (void)t;
+          }
+        }
+      }
+      const int row = row0 + 32 * sub + lane;
+      if (row < A.N) {
+#pragma unroll
+        for (int m = 0; m < MT; ++m)
+          if (m < A.M) store_out(A.out, A.out_dtype, (int64_t)m * A.out_stride + row, accm[m]);
+      }
+    } else if (ok) {
       float d[NBT];
 #pragma unroll
       for (int i = 0; i < NBT; ++i) d[i] = 0.f;
@@ -707,27 +749,31 @@ __global__ void __launch_bounds__(kThreads, 1) mx8_tc_kernel(const __grid_consta
     }
     tc_fence_before();
   } else {
-    // ---------------- activations -> e4m3 terms (warps 2..7), slab by slab ----------------
-    const int ptid = threadIdx.x - 64, pthreads = 192;
+    // ---------------- activations -> e4m3 terms (warps 2..7, and 12.. at 9-16 tokens), slab by slab ----------------
+    const int ptid = warp < 8 ? threadIdx.x - 64 : threadIdx.x - 192, pthreads = 192 + 32 * mx_prep_extra(MT);
     pdl_wait();
     const __nv_bfloat16* xr = reinterpret_cast<const __nv_bfloat16*>(base + A.smem_xraw);
-    if (ptid == 0) {
-      const uint32_t bytes = (uint32_t)A.K * 2u;
-      mbar_arrive_expect_tx(xbar, bytes * (uint32_t)MT);
-      for (int m = 0; m < MT; ++m)
-        bulk_g2s(smem_u32(base + A.smem_xraw) + m * bytes, A.x + (int64_t)m * A.x_stride, bytes, xbar);
+    if constexpr (!kXGlobal) {
+      if (ptid == 0) {
+        const uint32_t bytes = (uint32_t)A.K * 2u;
+        mbar_arrive_expect_tx(xbar, bytes * (uint32_t)MT);
+        for (int m = 0; m < MT; ++m)
+          bulk_g2s(smem_u32(base + A.smem_xraw) + m * bytes, A.x + (int64_t)m * A.x_stride, bytes, xbar);
+      }
+      if (!mbar_wait_bounded(xbar, 0, A.err)) ok = false;
     }
-    if (!mbar_wait_bounded(xbar, 0, A.err)) ok = false;
     uint8_t* bsm = base + A.smem_b;
     uint8_t* sfb = base + A.smem_sfb;
     for (int idx = ptid; idx < nstages * kBlkPerSlab; idx += pthreads) {
       const int slab = idx / kBlkPerSlab, rem = idx - slab * kBlkPerSlab;
       const int m = rem >> 2, jb = rem & 3, k0 = slab * kMxKC + jb * 32;
-      if (ok) {
+      // tokens beyond A.M (MT > 8): their B columns reach only output columns that are not stored
+      if (ok && (!kXGlobal || m < A.M)) {
         float v[32];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-          const uint4 w = reinterpret_cast<const uint4*>(xr + (int64_t)m * A.K + k0)[q];
+          const uint4 w = kXGlobal ? __ldcg(reinterpret_cast<const uint4*>(A.x + (int64_t)m * A.x_stride + k0) + q)
+                                   : reinterpret_cast<const uint4*>(xr + (int64_t)m * A.K + k0)[q];
           const uint32_t w4[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
           for (int e = 0; e < 4; ++e) {

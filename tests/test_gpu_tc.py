@@ -1,6 +1,5 @@
-"""GPU parity of the tcgen05 NVFP4 and MXFP8 GEMVs (shapes with at least 8,192 rows and M <= 16 tokens for NVFP4, M <= 8
-for MXFP8, take the block-scaled tensor-core kernel; the others take the register-decode kernel, covered in
-test_gpu_gemv.py).
+"""GPU parity of the tcgen05 NVFP4 and MXFP8 GEMVs (shapes with at least 8,192 rows and M <= 16 tokens take the
+block-scaled tensor-core kernel; the others take the register-decode kernel, covered in test_gpu_gemv.py).
 
 The tensor-core kernel multiplies the stored e2m1 weights and e4m3 scales exactly and writes each activation as six
 e2m1 terms with e4m3 block scales; what the terms leave out is below 9e-5 of the token's largest element.
@@ -130,6 +129,29 @@ def test_mx8_tc_matches_oracle(mx8_weights, m):
     cd, sd, xd = codes.to(DEV), sc.to(DEV), x.to(DEV)
     y32 = F.mx8_linear(xd, cd, sd, None, out_dtype=torch.float32).cpu()
     assert rel_err(y32, ref) < 2e-4
+    y16 = F.mx8_linear(xd, cd, sd, None).float().cpu()
+    assert rel_err(y16, ref) < 1e-2
+    assert torch.equal(F.mx8_linear(xd, cd, sd, None, out_dtype=torch.float32).cpu(), y32)
+
+
+@pytest.mark.parametrize("m", [9, 12, 13, 16])
+def test_mx8_tc_16_tokens_matches_oracle(mx8_weights, m):
+    """9..16 tokens on the 12- / 16-token kernels (activations read through L2, chunked epilogue), with a zero token
+    and a tiny one among them."""
+    codes, sc, wdeq = mx8_weights
+    g = torch.Generator().manual_seed(600 + m)
+    x = torch.randn(m, K, generator=g)
+    x[1] = 0.0
+    x[m - 1] *= 1e-6
+    x = x.to(torch.bfloat16)
+    ref = x.double().numpy() @ wdeq.T
+    cd, sd, xd = codes.to(DEV), sc.to(DEV), x.to(DEV)
+    y32 = F.mx8_linear(xd, cd, sd, None, out_dtype=torch.float32).cpu()
+    for i in range(m):
+        if i == 1:
+            assert torch.all(y32[1] == 0.0)
+        else:
+            assert rel_err(y32[i], ref[i]) < 2e-4, i
     y16 = F.mx8_linear(xd, cd, sd, None).float().cpu()
     assert rel_err(y16, ref) < 1e-2
     assert torch.equal(F.mx8_linear(xd, cd, sd, None, out_dtype=torch.float32).cpu(), y32)
