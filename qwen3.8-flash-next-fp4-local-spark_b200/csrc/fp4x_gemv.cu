@@ -350,7 +350,9 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
     // operand panel + raw panel (W8 copies the rows straight into the operand panel: no raw panel)
     const int xbytes = round_up(c.MP * c.XP, 16) + (c.xdirect || fmt == FMT_W8 ? 0 : (int)M * kpw * 2);
     const int fixed = xbytes + misc + scr_bytes + comb_bytes + 1024;
-    for (int cps = 2; cps >= 1; --cps) {
+    // 16-token plans keep one CTA per SM (the 128-register entry): at two per SM their stage bodies spill (the 48
+    // router gates at M = 16: 46 against 62 µs)
+    for (int cps = pl.NT == 2 ? 1 : 2; cps >= 1; --cps) {
       const int cap = cps == 2 ? cap2 : cap1;
       int ns = (cap - fixed) / c.STG;
       if (ns > kMaxStages) ns = kMaxStages;
