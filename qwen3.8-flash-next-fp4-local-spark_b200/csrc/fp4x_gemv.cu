@@ -246,7 +246,8 @@ static bool make_cluster_plan(int fmt, int64_t M, int64_t N, int64_t K, int grou
   const int misc = 512;
   const int comb_bytes = kRW * 32 * base.NT * 4 * 4;
   for (int KP = 8; KP >= 2; --KP) {
-    if (K % KP || (int64_t)base.RT * KP > 2 * dv.sms) continue;
+    // at 16 tokens one CTA per SM (the 128-register entry: the two-per-SM stage bodies spill)
+    if (K % KP || (int64_t)base.RT * KP > (base.NT == 2 ? 1 : 2) * dv.sms) continue;
     const int kpw = (int)(K / KP);
     int KC, BI0, NB0;
     if (kpw % 64 || !chunk_for(fmt, kpw, KC, BI0, NB0)) continue;
@@ -350,9 +351,10 @@ static int make_plan(int fmt, int64_t M, int64_t N, int64_t K, int64_t batch, in
     // operand panel + raw panel (W8 copies the rows straight into the operand panel: no raw panel)
     const int xbytes = round_up(c.MP * c.XP, 16) + (c.xdirect || fmt == FMT_W8 ? 0 : (int)M * kpw * 2);
     const int fixed = xbytes + misc + scr_bytes + comb_bytes + 1024;
-    // 16-token plans keep one CTA per SM (the 128-register entry): at two per SM their stage bodies spill (the 48
-    // router gates at M = 16: 46 against 62 µs)
-    for (int cps = pl.NT == 2 ? 1 : 2; cps >= 1; --cps) {
+    // 16-token stream-K plans keep one CTA per SM (the 128-register entry): at two per SM their stage bodies spill
+    // (the 48 router gates at M = 16: 46 against 62 µs).  Whole-tile plans (HC up) keep the choice: with more row
+    // blocks than SMs, one CTA per SM leaves some SMs two blocks in a row (the mixer at M = 16: 20.4 against 18.2 µs).
+    for (int cps = (pl.NT == 2 && !whole) ? 1 : 2; cps >= 1; --cps) {
       const int cap = cps == 2 ? cap2 : cap1;
       int ns = (cap - fixed) / c.STG;
       if (ns > kMaxStages) ns = kMaxStages;
