@@ -93,7 +93,7 @@ int fp4x_mx8_linear(const void* x, int64_t x_stride, const void* w, const void* 
                     int64_t n_counters, void* stream);
 
 /* MXFP8 GEMV that allocates nothing and takes no scratch (no counterpart in the reference).  It always runs the
- * register-decode split-K kernel; fp4x_mx8_linear sends M <= 8 at 8192 rows or more to the tensor-core kernel, so
+ * register-decode split-K kernel; fp4x_mx8_linear sends M <= 16 at 8192 rows or more to the tensor-core kernel, so
  * the two agree to fp32 summation order.  For callers that cannot hand the library a workspace or allocate device
  * memory at call time, such as a host runtime without a caching allocator.  The split-K scratch is a static
  * device array of the library: 8 MiB of partial tiles and 32768 int32 arrival counters per device.  Shapes whose

@@ -17,7 +17,7 @@
 // exact and accumulate in fp32).  The epilogue recombines the term columns with the factors 2^(e0 - 2t).
 //
 // Roles (384 threads; 576 at 5-8 tokens, 704 at 9-16): warp 0 streams weight tiles and their scale tiles (TMA); warp 1 owns the
-// tensor memory and one of its lanes issues the MMAs; warps 2..7 (and 12..17 at 5-8 tokens) turn the activations into
+// tensor memory and one of its lanes issues the MMAs; warps 2..7 (and 12.. at 5-16 tokens) turn the activations into
 // e2m1 terms after the grid-dependency wait, slab by slab (256 k), so the MMAs of the first slabs start while later
 // slabs are still being prepared; warps 8..11 (tensor-memory subpartitions 0..3) write each stage's A scales and
 // each slab's B scales into tensor memory from registers, running ahead of the MMAs, and then run the epilogue.
